@@ -1,0 +1,99 @@
+"""ctypes binding of libaxq8.so, the C ABI declared in include/axq8.h.
+
+Loading fails loudly: there is no CPU fallback for any entry point.  If the
+shared library is missing, build it with ``python -m axion_b200.build``.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+_LIB_PATH = Path(__file__).resolve().parent / "libaxq8.so"
+
+AXQ8_OK = 0
+AXQ8_ERR_INVALID = -1
+AXQ8_ERR_CUDA = -2
+AXQ8_ERR_ALLOC = -3
+AXQ8_ERR_WAIT_TIMEOUT = -4
+AXQ8_ERR_UNSUPPORTED = -5
+AXQ8_ERR_STATE = -6
+
+AXQ8_ACT_Q8 = 0
+AXQ8_ACT_F32 = 1
+
+
+class axq8_weight_t(C.Structure):
+    _fields_ = [
+        ("rows", C.c_void_p),
+        ("N", C.c_int64),
+        ("K", C.c_int64),
+        ("row_stride", C.c_int64),
+        ("owns", C.c_int32),
+        ("device", C.c_int32),
+    ]
+
+
+_P = C.c_void_p
+_I64 = C.c_int64
+_I32 = C.c_int
+_W = C.POINTER(axq8_weight_t)
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "axq8_q8_0_byte_size": (C.c_uint64, [C.c_uint64]),
+    "axq8_row_stride": (_I64, [_I64]),
+    "axq8_weight_upload": (_I32, [_P, _I64, _I64, _P, _W]),
+    "axq8_weight_repack": (_I32, [_P, _I64, _I64, _P, _P]),
+    "axq8_weight_wrap": (_I32, [_P, _I64, _I64, _W]),
+    "axq8_weight_free": (_I32, [_W]),
+    "axq8_dequantize": (_I32, [_W, _P, _P]),
+    "axq8_quantize_act": (_I32, [_P, _I64, _I64, _P, _P, _P]),
+    "axq8_linear": (_I32, [_W, _P, _I64, _P, _I32, _P]),
+    "axq8_linear_q8act": (_I32, [_W, _P, _P, _I64, _P, _P, _P]),
+    "axq8_block_dots": (_I32, [_W, _P, _I64, _P, _P]),
+    "axq8_quantize_weight_tensor": (_I32, [_P, _I64, _I64, _P, _P, _P]),
+    "axq8_quantized_matmul": (_I32, [_P, _I64, _I64, _P, _P, _I64, _P, _P]),
+    "axq8_synth_q8_0": (_I32, [C.c_uint64, _I64, _I64, C.c_float, C.c_float, _I32, _P, _P]),
+    "axq8_status_read": (_I32, [C.POINTER(C.c_int)]),
+    "axq8_status_clear": (_I32, []),
+    "axq8_last_error": (C.c_char_p, []),
+    "axq8_version": (C.c_char_p, []),
+}
+
+_lib: C.CDLL | None = None
+
+
+def lib_path() -> Path:
+    return _LIB_PATH
+
+
+def load() -> C.CDLL:
+    """Load libaxq8.so and declare every exported signature."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not _LIB_PATH.exists():
+        raise RuntimeError(
+            f"axion_b200: CUDA library {_LIB_PATH} is missing; "
+            "build it with `python -m axion_b200.build` (no CPU fallback exists)")
+    lib = C.CDLL(str(_LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = lib
+    return lib
+
+
+class AxionCudaError(RuntimeError):
+    """A C-ABI call returned a negative status."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(msg)
+        self.code = code
+
+
+def check(rc: int) -> None:
+    if rc != AXQ8_OK:
+        msg = load().axq8_last_error().decode(errors="replace")
+        raise AxionCudaError(rc, msg or f"axion_b200 error {rc}")

@@ -1,0 +1,102 @@
+"""Build libaxq8.so (the C-ABI library) in-tree for sm_100a with nvcc.
+
+Usage: python -m axion_b200.build [--force] [-j N]
+
+Every ``axion_b200/csrc/*.cu`` / ``*.cpp`` is compiled to an object under
+``axion_b200/_build/`` and linked into ``axion_b200/libaxq8.so``.  The CUDA
+runtime is linked statically so the library does not depend on which
+libcudart the host process (e.g. torch) has loaded; both share the device's
+primary context, so device pointers and streams pass freely between them.
+"""
+from __future__ import annotations
+
+import argparse
+import concurrent.futures as cf
+import os
+import shutil
+import subprocess
+import sys
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+ROOT = PKG.parent
+CSRC = PKG / "csrc"
+BUILD = PKG / "_build"
+LIB = PKG / "libaxq8.so"
+
+ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
+NVCC_FLAGS = ARCH + [
+    "-O3", "-lineinfo", "-std=c++17", "--expt-relaxed-constexpr",
+    "-Xcompiler", "-fPIC,-O3", "-Xptxas", "-O3",
+    f"-I{ROOT / 'include'}", f"-I{CSRC}",
+]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", shutil.which("nvcc")):
+        if cand and Path(cand).exists():
+            return cand
+    raise RuntimeError("nvcc not found")
+
+
+def nccl_include() -> list[str]:
+    """NCCL header location (torch's bundled NCCL, else the system one)."""
+    try:
+        import nvidia.nccl  # type: ignore
+        inc = Path(list(nvidia.nccl.__path__)[0]) / "include"
+        if (inc / "nccl.h").exists():
+            return [f"-I{inc}"]
+    except Exception:
+        pass
+    return []
+
+
+def sources() -> list[Path]:
+    return sorted(list(CSRC.glob("*.cu")) + list(CSRC.glob("*.cpp")))
+
+
+def _headers_mtime() -> float:
+    hs = list(CSRC.glob("*.cuh")) + list(CSRC.glob("*.h")) + list((ROOT / "include").glob("*.h"))
+    return max((h.stat().st_mtime for h in hs), default=0.0)
+
+
+def _compile(src: Path, force: bool, hdr_mtime: float) -> Path:
+    obj = BUILD / (src.name + ".o")
+    if (not force and obj.exists() and obj.stat().st_mtime >= src.stat().st_mtime
+            and obj.stat().st_mtime >= hdr_mtime):
+        return obj
+    cmd = [nvcc(), *NVCC_FLAGS, *nccl_include(), "-c", str(src), "-o", str(obj)]
+    if src.suffix == ".cpp":
+        cmd[1:1] = ["-x", "cu"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"nvcc failed for {src.name}:\n{r.stdout}\n{r.stderr}")
+    return obj
+
+
+def build(force: bool = False, jobs: int | None = None) -> Path:
+    BUILD.mkdir(exist_ok=True)
+    srcs = sources()
+    hm = _headers_mtime()
+    with cf.ThreadPoolExecutor(max_workers=jobs or min(8, os.cpu_count() or 4)) as ex:
+        objs = list(ex.map(lambda s: _compile(s, force, hm), srcs))
+    newest = max(o.stat().st_mtime for o in objs)
+    if force or not LIB.exists() or LIB.stat().st_mtime < newest:
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+    return LIB
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--force", action="store_true")
+    ap.add_argument("-j", type=int, default=None)
+    args = ap.parse_args()
+    print(build(args.force, args.j))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

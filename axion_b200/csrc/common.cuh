@@ -1,0 +1,139 @@
+// Shared device helpers for the Q8_0 kernels (sm_100a only).
+//
+// Inline PTX wrappers for mbarriers, 1-D bulk async copies (TMA engine,
+// non-tensor form, no multicast), programmatic dependent launch, and the
+// bounded-wait discipline every spin in this library follows: a wait gives up
+// after a fixed clock budget, records an error code in the device status word
+// and lets the kernel return, so a lost arrival can never hang the GPU.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "axq8_status.h"
+
+#if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
+#error "axion_b200 kernels target sm_100a only"
+#endif
+
+namespace axq8 {
+
+constexpr int QK = 32;                 // elements per Q8_0 block
+constexpr int Q8_0_BYTES = 34;         // fp16 d + 32 int8 (GGUF on-disk block)
+
+// Device row layout of a repacked Q8_0 weight ("Q8R"): for every output row
+// n, K int8 quants, then K/32 fp16 scales, then zero padding to 16 bytes.
+// One row is therefore one 16-byte-aligned contiguous span that a single
+// bulk copy can move, and the whole [N, K] weight is a 2-D array with a
+// 16-byte-multiple row stride (a valid TMA tensor map for the quants).
+__host__ __device__ inline int64_t q8r_scale_bytes(int64_t K) {
+    return (((K / QK) * 2) + 15) / 16 * 16;
+}
+__host__ __device__ inline int64_t q8r_row_stride(int64_t K) {
+    return K + q8r_scale_bytes(K);
+}
+
+// Wall-clock budget of any bounded wait, in SM clock cycles (~1 s at 2 GHz).
+constexpr long long WAIT_BUDGET_CYCLES = 2000000000LL;
+
+__device__ inline uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ inline void record_status(int* status, int code) {
+    if (status) atomicCAS(status, 0, code);
+}
+
+// ---- mbarrier -------------------------------------------------------------
+
+__device__ inline void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
+                 : "memory");
+}
+
+__device__ inline void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ inline void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ inline void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ inline bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete.  Returns
+// false (and records `code`) when the budget runs out.
+__device__ inline bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status,
+                                         int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (true) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (clock64() - t0 > WAIT_BUDGET_CYCLES) {
+            record_status(status, code);
+            return false;
+        }
+    }
+}
+
+// ---- 1-D bulk copy global -> shared (TMA engine, no tensor map) -----------
+// Both addresses 16-byte aligned, size a multiple of 16.  Completion is
+// signalled as transaction bytes on `bar`.
+__device__ inline void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t bytes,
+                                uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(smem_u32(smem_dst)),
+        "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// ---- programmatic dependent launch ----------------------------------------
+// wait: block until the preceding grid in the stream has completed and its
+// writes are visible (no-op when the launch had no programmatic edge).
+__device__ inline void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+// launch_dependents: allow the next grid to start launching its CTAs.
+__device__ inline void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" :::);
+}
+
+// ---- small numeric helpers -------------------------------------------------
+
+__device__ inline float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+__device__ inline float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Round half away from zero and clamp to the symmetric int8 range; the
+// activation quantizer's rounding rule (C99 roundf semantics).
+__device__ inline int q8_round(float v) {
+    float r = roundf(v);
+    r = fminf(fmaxf(r, -127.0f), 127.0f);
+    return static_cast<int>(r);
+}
+
+}  // namespace axq8

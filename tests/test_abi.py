@@ -1,0 +1,77 @@
+"""The C-ABI library loads and exports every function its headers declare.
+
+No compute call is made here (no GPU needed).
+"""
+from __future__ import annotations
+
+import ctypes
+import re
+import subprocess
+
+from conftest import ROOT
+
+HEADERS = sorted((ROOT / "include").glob("*.h"))
+DECL = re.compile(r"^[A-Za-z_][\w \t\*]*?\b(ax[a-z0-9]*_\w+)\s*\(", re.M)
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for h in HEADERS:
+        text = h.read_text()
+        text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+        names.update(DECL.findall(text))
+    return names
+
+
+def test_headers_declare_functions():
+    names = declared_functions()
+    assert "axq8_linear" in names and "axq8_weight_upload" in names
+    assert len(names) >= 15
+
+
+def test_library_exports_every_declared_symbol():
+    from axion_b200 import _lib
+    lib = _lib.load()
+    missing = [n for n in sorted(declared_functions()) if not hasattr(lib, n)]
+    assert not missing, f"declared but not exported: {missing}"
+
+
+def test_bindings_cover_declarations():
+    from axion_b200 import _lib
+    missing = sorted(declared_functions() - set(_lib.SIGNATURES))
+    assert not missing, f"no ctypes signature for: {missing}"
+
+
+def test_library_is_sm100a_only():
+    """The fatbin carries sm_100a code only (no PTX, no other SM)."""
+    so = ROOT / "axion_b200" / "libaxq8.so"
+    r = subprocess.run(["cuobjdump", "--list-elf", str(so)], capture_output=True, text=True)
+    if r.returncode != 0:
+        import pytest
+        pytest.skip("cuobjdump unavailable")
+    arches = set(re.findall(r"sm_(\d+a?)", r.stdout))
+    assert arches == {"100a"}, arches
+
+
+def test_pure_host_entry_points():
+    """Size helpers need no device."""
+    from axion_b200 import _lib
+    lib = _lib.load()
+    assert lib.axq8_q8_0_byte_size(32) == 34
+    assert lib.axq8_q8_0_byte_size(5632 * 2048) == 12_255_232
+    assert lib.axq8_row_stride(2048) == 2048 + 128
+    assert lib.axq8_row_stride(32) == 32 + 16
+    assert lib.axq8_row_stride(5632) % 16 == 0
+    assert b"sm_100a" in lib.axq8_version()
+
+
+def test_invalid_arguments_fail_cleanly():
+    """Argument validation runs before any device work and reports a message."""
+    from axion_b200 import _lib
+    lib = _lib.load()
+    w = _lib.axq8_weight_t()
+    rc = lib.axq8_weight_wrap(None, 4, 33, ctypes.byref(w))
+    assert rc == _lib.AXQ8_ERR_INVALID
+    assert b"K" in lib.axq8_last_error() or b"null" in lib.axq8_last_error()
+    rc = lib.axq8_linear(None, None, 1, None, 0, None)
+    assert rc == _lib.AXQ8_ERR_INVALID
