@@ -190,10 +190,8 @@ __global__ void synth_q8_0_kernel(uint64_t seed, int64_t N, int64_t K, float mea
         const __half dh = __float2half_rn(d);
         uint8_t* qdst;
         if (layout == 0) {
-            uint8_t* blk = out + t * Q8_0_BYTES;
-            const uint16_t bits = __half_as_ushort(dh);
-            blk[0] = (uint8_t)(bits & 0xff);
-            blk[1] = (uint8_t)(bits >> 8);
+            uint8_t* blk = out + t * Q8_0_BYTES;   // even offset: 2-byte aligned
+            *reinterpret_cast<uint16_t*>(blk) = __half_as_ushort(dh);
             qdst = blk + 2;
         } else {
             uint8_t* row = out + n * rs;

@@ -60,6 +60,16 @@ def measured_peaks() -> tuple[dict, str]:
     return {"hbm_gbs": FALLBACK_HBM_GBS, "bf16_tflops": FALLBACK_BF16_TFLOPS}, "fallback"
 
 
+def ncu_traffic(workload: str):
+    """DRAM bytes per launch of the dominant kernel from the committed ncu
+    summary (profiles/ncu_traffic.json), or None."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    try:
+        return json.loads(p.read_text())[workload]["traffic_bytes"]
+    except Exception:
+        return None
+
+
 def host_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -196,6 +206,9 @@ def run_gemv_axion(args, d: Dist) -> dict:
     dev = torch.device("cuda", d.local)
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(dev)
+    # Every launch, graph replay, copy and event of this arm goes on `stream`
+    # (CUDAGraph.replay() launches on the current stream).
+    torch.cuda.set_stream(stream)
     props = torch.cuda.get_device_properties(dev)
     l2 = getattr(props, "L2_cache_size", 126 * 2**20)
     wbytes = GEMV_N * ops.row_stride(GEMV_K)
@@ -266,7 +279,7 @@ def run_gemv_axion(args, d: Dist) -> dict:
     achieved = alg / (k_ms / 1e3) / 1e9
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": None, "kernel": "q8_gemv_kernel<1,false>",
+                "traffic": ncu_traffic("q8_gemv_5632x2048_m1"), "kernel": "q8_gemv_kernel<1,0,0>",
                 "kernel_us": round(k_ms * 1e3, 3), "peak_source": peak_kind,
                 "algorithmic_bytes": alg}
 
