@@ -50,6 +50,7 @@ SIGNATURES: dict[str, tuple] = {
     "axq8_quantize_act": (_I32, [_P, _I64, _I64, _P, _P, _P]),
     "axq8_linear": (_I32, [_W, _P, _I64, _P, _I32, _P]),
     "axq8_linear_q8act": (_I32, [_W, _P, _P, _I64, _P, _P, _P]),
+    "axq8_linear_noalloc": (_I32, [_W, _P, _I64, _P, _P]),
     "axq8_block_dots": (_I32, [_W, _P, _I64, _P, _P]),
     "axq8_quantize_weight_tensor": (_I32, [_P, _I64, _I64, _P, _P, _P]),
     "axq8_quantized_matmul": (_I32, [_P, _I64, _I64, _P, _P, _I64, _P, _P]),

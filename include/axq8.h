@@ -101,6 +101,20 @@ int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int
 int axq8_linear_q8act(const axq8_weight_t* w, const int8_t* xq, const float* dx, int64_t M,
                       const float* residual, float* y, void* stream);
 
+/* axq8_linear in A8 mode for callers that cannot allocate device memory:
+ * code running under a fixed, pre-planned memory budget (an allocator that
+ * owns all of HBM) or code that must not risk the device synchronization
+ * cudaMalloc/cudaFree can cause.  No counterpart in the reference (its
+ * linear runs on the host).  Allocates nothing: the quantized activation
+ * goes to a fixed 1.125 MiB static device array that every GPU loading this
+ * library reserves until exit.  Limit: M*K <= 1,048,576, else
+ * AXQ8_ERR_INVALID.  The array is shared by all calls on a device: calls
+ * that overlap on the GPU race and must be serialized by the caller.  The
+ * first call on a device looks up the array's address; make it before any
+ * stream capture. */
+int axq8_linear_noalloc(const axq8_weight_t* w, const float* x, int64_t M, float* y,
+                        void* stream);
+
 /* Exact int32 block dot products dots[M, N, K/32] = sum_i qw*qx over each
  * 32-block; a debug/parity entry point (slow). */
 int axq8_block_dots(const axq8_weight_t* w, const int8_t* xq, int64_t M, int32_t* dots,
