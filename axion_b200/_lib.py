@@ -33,6 +33,16 @@ class axq8_weight_t(C.Structure):
     ]
 
 
+class axdec_config_t(C.Structure):
+    _fields_ = [
+        ("n_layers", C.c_int32), ("hidden", C.c_int32), ("ffn", C.c_int32),
+        ("n_heads", C.c_int32), ("n_kv_heads", C.c_int32), ("head_dim", C.c_int32),
+        ("vocab", C.c_int32), ("rope_theta", C.c_float), ("rms_eps", C.c_float),
+        ("max_batch", C.c_int32), ("max_ctx", C.c_int32), ("kv_block", C.c_int32),
+        ("act_mode", C.c_int32), ("kv_fp32", C.c_int32),
+    ]
+
+
 _P = C.c_void_p
 _I64 = C.c_int64
 _I32 = C.c_int
@@ -55,6 +65,15 @@ SIGNATURES: dict[str, tuple] = {
     "axq8_quantize_weight_tensor": (_I32, [_P, _I64, _I64, _P, _P, _P]),
     "axq8_quantized_matmul": (_I32, [_P, _I64, _I64, _P, _P, _I64, _P, _P]),
     "axq8_synth_q8_0": (_I32, [C.c_uint64, _I64, _I64, C.c_float, C.c_float, _I32, _P, _P]),
+    "axdec_create": (_I32, [C.POINTER(axdec_config_t), C.POINTER(C.c_void_p)]),
+    "axdec_destroy": (_I32, [_P]),
+    "axdec_set_tensor": (_I32, [_P, C.c_char_p, _P, _I32, _I64, _I64]),
+    "axdec_init_random": (_I32, [_P, C.c_uint64, C.c_float]),
+    "axdec_tensor_index": (_I32, [C.POINTER(axdec_config_t), C.c_char_p]),
+    "axdec_generate": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P, C.POINTER(C.c_float), _P]),
+    "axdec_forced": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P]),
+    "axdec_device_bytes": (_I64, [_P]),
+    "axdec_weight_bytes_per_step": (_I64, [_P]),
     "axq8_status_read": (_I32, [C.POINTER(C.c_int)]),
     "axq8_status_clear": (_I32, []),
     "axq8_last_error": (C.c_char_p, []),

@@ -1,0 +1,616 @@
+// Llama-architecture decode step on B200 built from the Q8_0 GEMV (C ABI in
+// include/axdec.h).
+//
+// One step processes one position of each of M sequences:
+//   embed -> per layer [ rmsnorm(+q8) -> GEMV qkv -> rope + KV page append
+//   -> split-K attention -> combine(+q8) -> GEMV o (+residual, in place)
+//   -> rmsnorm(+q8) -> GEMV gate|up -> silu*up(+q8) -> GEMV down (+residual) ]
+//   -> rmsnorm(+q8) -> GEMV lm_head -> argmax + advance
+// the order of StreamingExecutor::decode_layer (streaming_executor.cpp:268-401)
+// and ModelRunner::generate (model_runner.cpp:245-317).  Q, K and V share one
+// fused weight (rows of attn_q, attn_k, attn_v stacked) and so do gate and up,
+// so each layer streams its weights in four GEMVs.  All kernels are launched
+// with programmatic dependent launch and the whole step is captured once in a
+// CUDA graph per batch size; the control state (positions, input tokens, fed
+// tokens) lives in device memory so the same graph serves every step.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+#include <algorithm>
+#include <cmath>
+#include <map>
+#include <string>
+#include <vector>
+
+#include "axdec.h"
+#include "axq8.h"
+#include "common.cuh"
+#include "decode_ops.cuh"
+#include "q8_gemv.cuh"
+#include "runtime.h"
+
+using namespace axq8;
+
+namespace {
+
+constexpr int kNormThreads = 256;
+
+struct Layer {
+    uint8_t* qkv = nullptr;    // [Nq + 2 Nkv, H] Q8R
+    uint8_t* o = nullptr;      // [H, Nq]
+    uint8_t* gu = nullptr;     // [2F, H]
+    uint8_t* down = nullptr;   // [H, F]
+    float* attn_norm = nullptr;
+    float* ffn_norm = nullptr;
+    void* kc = nullptr;        // [pages][n_kv][B][hd]
+    void* vc = nullptr;
+};
+
+struct Graph {
+    cudaGraphExec_t exec = nullptr;
+};
+
+}  // namespace
+
+struct axdec_model {
+    axdec_config_t c{};
+    DeviceState* ds = nullptr;
+    int Nq = 0, Nkv = 0, Nqkv = 0;
+    int64_t rs_h = 0, rs_q = 0, rs_f = 0;
+    std::vector<void*> allocs;
+    int64_t bytes = 0;
+    uint8_t* embd = nullptr;      // [V, H]
+    uint8_t* out_w = nullptr;     // [V, H] (== embd when tied)
+    bool out_set = false;
+    float* out_norm = nullptr;
+    std::vector<Layer> L;
+    int max_blocks = 0, nsplit = 1, bps = 1;
+    // activations
+    float* h = nullptr;           // [M, H] residual stream
+    int8_t* xq = nullptr;         // [M, maxK]
+    float* dx = nullptr;          // [M, maxK/32]
+    float* x32 = nullptr;         // [M, maxK] (A32 mode)
+    float* qkv = nullptr;         // [M, Nqkv]
+    float* gu = nullptr;          // [M, 2F]
+    float* part = nullptr;        // attention partials
+    float* logits = nullptr;      // [M, V]
+    float2* rope = nullptr;       // [max_ctx, hd/2]
+    int* block_table = nullptr;   // [max_batch, max_blocks]
+    int* tokens = nullptr;        // [M]
+    int* pos = nullptr;           // [M]
+    int* feed = nullptr;          // [M, max_ctx]
+    int* out_tokens = nullptr;    // [M, max_ctx]
+    int* argmax = nullptr;        // [M]
+    int* ctl = nullptr;           // {n_prompt, feed_len, max_out}
+    cudaStream_t cap_stream = nullptr;
+    std::map<int, Graph> graphs;  // per batch size
+};
+
+namespace {
+
+void* dalloc(axdec_model* m, size_t bytes, int* rc) {
+    void* p = nullptr;
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) {
+        *rc = cuda_fail(e, "axdec: cudaMalloc");
+        return nullptr;
+    }
+    m->allocs.push_back(p);
+    m->bytes += (int64_t)bytes;
+    return p;
+}
+
+bool parse_layer_name(const char* name, int* layer, std::string* slot) {
+    if (strncmp(name, "blk.", 4) != 0) return false;
+    char* end = nullptr;
+    long l = strtol(name + 4, &end, 10);
+    if (end == name + 4 || *end != '.') return false;
+    std::string rest(end + 1);
+    const std::string suf = ".weight";
+    if (rest.size() <= suf.size() || rest.compare(rest.size() - suf.size(), suf.size(), suf) != 0)
+        return false;
+    *layer = (int)l;
+    *slot = rest.substr(0, rest.size() - suf.size());
+    return true;
+}
+
+const char* kSlots[9] = {"attn_norm", "attn_q", "attn_k", "attn_v", "attn_output",
+                         "ffn_norm", "ffn_gate", "ffn_up", "ffn_down"};
+
+int slot_index(const std::string& s) {
+    for (int i = 0; i < 9; i++)
+        if (s == kSlots[i]) return i;
+    return -1;
+}
+
+// Destination of a Q8_0 tensor: repacked rows, row offset, and expected shape.
+struct Dest {
+    uint8_t* rows = nullptr;
+    int64_t row0 = 0, N = 0, K = 0;
+    float* f32 = nullptr;   // norm weight destination
+    int64_t n = 0;
+};
+
+int resolve(axdec_model* m, const char* name, Dest* d) {
+    const axdec_config_t& c = m->c;
+    const int H = c.hidden, F = c.ffn;
+    if (!strcmp(name, "token_embd.weight")) { *d = {m->embd, 0, c.vocab, H}; return 0; }
+    if (!strcmp(name, "output.weight")) { *d = {m->out_w, 0, c.vocab, H}; return 0; }
+    if (!strcmp(name, "output_norm.weight")) { d->f32 = m->out_norm; d->n = H; return 0; }
+    int layer;
+    std::string slot;
+    if (!parse_layer_name(name, &layer, &slot) || layer < 0 || layer >= c.n_layers)
+        return fail(AXQ8_ERR_INVALID, "axdec: unknown tensor '%s'", name);
+    Layer& Ly = m->L[layer];
+    const int si = slot_index(slot);
+    switch (si) {
+        case 0: d->f32 = Ly.attn_norm; d->n = H; return 0;
+        case 5: d->f32 = Ly.ffn_norm; d->n = H; return 0;
+        case 1: *d = {Ly.qkv, 0, m->Nq, H}; return 0;
+        case 2: *d = {Ly.qkv, m->Nq, m->Nkv, H}; return 0;
+        case 3: *d = {Ly.qkv, m->Nq + m->Nkv, m->Nkv, H}; return 0;
+        case 4: *d = {Ly.o, 0, H, m->Nq}; return 0;
+        case 6: *d = {Ly.gu, 0, F, H}; return 0;
+        case 7: *d = {Ly.gu, F, F, H}; return 0;
+        case 8: *d = {Ly.down, 0, H, F}; return 0;
+        default: return fail(AXQ8_ERR_INVALID, "axdec: unknown tensor '%s'", name);
+    }
+}
+
+__global__ void fill_kernel(float* p, int64_t n, float v) {
+    for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n;
+         i += (int64_t)gridDim.x * blockDim.x)
+        p[i] = v;
+}
+
+template <typename KV>
+int launch_step_kv(axdec_model* m, int M, cudaStream_t s);
+
+int launch_step(axdec_model* m, int M, cudaStream_t s) {
+    return m->c.kv_fp32 ? launch_step_kv<float>(m, M, s) : launch_step_kv<__half>(m, M, s);
+}
+
+int gemv(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M, const float* resid,
+         float* y, cudaStream_t s) {
+    GemvArgs a = {};
+    a.rows = rows;
+    a.N = N;
+    a.K = K;
+    a.row_stride = q8r_row_stride(K);
+    a.M = M;
+    a.xq = m->xq;
+    a.dx = m->dx;
+    a.x = m->x32;
+    a.residual = resid;
+    a.y = y;
+    a.ldy = N;
+    a.status = m->ds->status;
+    return gemv_launch(m->ds, a, m->c.act_mode == AXQ8_ACT_F32, s);
+}
+
+template <typename KV, int HD>
+int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s) {
+    const axdec_config_t& c = m->c;
+    const int G = c.n_heads / c.n_kv_heads;
+    const size_t smem = (size_t)(2 * 16 + G) * HD * sizeof(float);
+    const float scale = 1.0f / std::sqrt((float)HD);   // mha.cpp:250
+    Layer& Ly = m->L[layer];
+    AXQ8_CUDA_TRY(launch_k(attn_partial_kernel<KV, HD>, dim3(c.n_kv_heads, M, m->nsplit),
+                           dim3(G * 32), smem, s, true, (const float*)m->qkv, m->Nqkv,
+                           (const int*)m->pos, (const KV*)Ly.kc, (const KV*)Ly.vc,
+                           (const int*)m->block_table, m->max_blocks, c.n_heads, c.n_kv_heads,
+                           m->bps, scale, m->part),
+                  "attn_partial launch");
+    const int warps = M * c.n_heads;
+    const int nb = (warps + 7) / 8;
+    if (c.act_mode == AXQ8_ACT_F32) {
+        AXQ8_CUDA_TRY(launch_k(attn_combine_kernel<HD, false>, dim3(nb), dim3(256), 0, s, true,
+                               (const float*)m->part, M, c.n_heads, m->nsplit, m->x32,
+                               (int8_t*)nullptr, (float*)nullptr),
+                      "attn_combine launch");
+    } else {
+        AXQ8_CUDA_TRY(launch_k(attn_combine_kernel<HD, true>, dim3(nb), dim3(256), 0, s, true,
+                               (const float*)m->part, M, c.n_heads, m->nsplit, (float*)nullptr,
+                               m->xq, m->dx),
+                      "attn_combine launch");
+    }
+    return AXQ8_OK;
+}
+
+int launch_rmsnorm(axdec_model* m, int M, const float* x, const float* w, cudaStream_t s) {
+    const axdec_config_t& c = m->c;
+    if (c.act_mode == AXQ8_ACT_F32) {
+        AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<false>, dim3(M), dim3(kNormThreads), 0, s, true, x, w,
+                               c.hidden, c.rms_eps, m->x32, (int8_t*)nullptr, (float*)nullptr),
+                      "rmsnorm launch");
+    } else {
+        AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<true>, dim3(M), dim3(kNormThreads), 0, s, true, x, w,
+                               c.hidden, c.rms_eps, (float*)nullptr, m->xq, m->dx),
+                      "rmsnorm launch");
+    }
+    return AXQ8_OK;
+}
+
+template <typename KV>
+int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
+    const axdec_config_t& c = m->c;
+    const int H = c.hidden, F = c.ffn, hd = c.head_dim;
+    int rc;
+    AXQ8_CUDA_TRY(launch_k(embed_kernel, dim3(M), dim3(256), 0, s, true, (const uint8_t*)m->embd,
+                           m->rs_h, H, c.vocab, (const int*)m->tokens, m->h, m->ds->status),
+                  "embed launch");
+    for (int l = 0; l < c.n_layers; l++) {
+        Layer& Ly = m->L[l];
+        if ((rc = launch_rmsnorm(m, M, m->h, Ly.attn_norm, s))) return rc;
+        if ((rc = gemv(m, Ly.qkv, m->Nqkv, H, M, nullptr, m->qkv, s))) return rc;
+        AXQ8_CUDA_TRY(launch_k(rope_kv_kernel<KV>, dim3(M), dim3(256), 0, s, true, m->qkv, m->Nqkv,
+                               (const int*)m->pos, (const float2*)m->rope, c.max_ctx, c.n_heads,
+                               c.n_kv_heads, hd, (KV*)Ly.kc, (KV*)Ly.vc,
+                               (const int*)m->block_table, m->max_blocks, c.kv_block,
+                               m->ds->status),
+                      "rope_kv launch");
+        if (hd == 32) rc = launch_attention<KV, 32>(m, M, l, s);
+        else if (hd == 64) rc = launch_attention<KV, 64>(m, M, l, s);
+        else rc = launch_attention<KV, 128>(m, M, l, s);
+        if (rc) return rc;
+        if ((rc = gemv(m, Ly.o, H, m->Nq, M, m->h, m->h, s))) return rc;
+        if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s))) return rc;
+        if ((rc = gemv(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu, s))) return rc;
+        const int nwarps = M * (F / QK);
+        if (c.act_mode == AXQ8_ACT_F32) {
+            AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, dim3((nwarps + 7) / 8), dim3(256), 0, s,
+                                   true, (const float*)m->gu, F, M, m->x32, (int8_t*)nullptr,
+                                   (float*)nullptr),
+                          "silu launch");
+        } else {
+            AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0, s,
+                                   true, (const float*)m->gu, F, M, (float*)nullptr, m->xq, m->dx),
+                          "silu launch");
+        }
+        if ((rc = gemv(m, Ly.down, H, F, M, m->h, m->h, s))) return rc;
+    }
+    if ((rc = launch_rmsnorm(m, M, m->h, m->out_norm, s))) return rc;
+    if ((rc = gemv(m, m->out_w, c.vocab, H, M, nullptr, m->logits, s))) return rc;
+    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3(M), dim3(512), 0, s, true,
+                           (const float*)m->logits, c.vocab, m->tokens, m->pos,
+                           (const int*)m->feed, (const int*)m->ctl, m->out_tokens, m->argmax),
+                  "argmax launch");
+    return AXQ8_OK;
+}
+
+// Instantiate (once per batch size) the graph of one decode step.  The first
+// time, the step runs eagerly once so every kernel is loaded and configured
+// before capture; the caller resets the control state afterwards.
+int get_graph(axdec_model* m, int M, cudaGraphExec_t* out) {
+    auto it = m->graphs.find(M);
+    if (it != m->graphs.end()) {
+        *out = it->second.exec;
+        return AXQ8_OK;
+    }
+    cudaStream_t s = m->cap_stream;
+    // warm-up from position 0 with the prompt/feed state left as is
+    AXQ8_CUDA_TRY(cudaMemsetAsync(m->pos, 0, sizeof(int) * m->c.max_batch, s), "axdec: pos reset");
+    int rc = launch_step(m, M, s);
+    if (rc) return rc;
+    AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec: warm-up step");
+    cudaGraph_t g = nullptr;
+    AXQ8_CUDA_TRY(cudaStreamBeginCapture(s, cudaStreamCaptureModeThreadLocal), "axdec: begin capture");
+    rc = launch_step(m, M, s);
+    cudaError_t e = cudaStreamEndCapture(s, &g);
+    if (rc) {
+        if (g) cudaGraphDestroy(g);
+        return rc;
+    }
+    if (e != cudaSuccess) return cuda_fail(e, "axdec: end capture");
+    cudaGraphExec_t exec = nullptr;
+    e = cudaGraphInstantiate(&exec, g, 0);
+    cudaGraphDestroy(g);
+    if (e != cudaSuccess) return cuda_fail(e, "axdec: graph instantiate");
+    m->graphs[M].exec = exec;
+    *out = exec;
+    return AXQ8_OK;
+}
+
+// Reset the control state for a run: positions 0, fed tokens uploaded, first
+// input = feed[:, 0].
+int reset_run(axdec_model* m, const int32_t* feed_host, int M, int feed_len, int n_prompt,
+              int max_out, cudaStream_t s) {
+    const int mc = m->c.max_ctx;
+    if (feed_len > mc) return fail(AXQ8_ERR_INVALID, "axdec: %d positions > max_ctx %d", feed_len, mc);
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->feed, feed_host, sizeof(int) * (size_t)M * feed_len,
+                                  cudaMemcpyHostToDevice, s), "axdec: feed upload");
+    std::vector<int> first(M), zeros(M, 0);
+    for (int i = 0; i < M; i++) first[i] = feed_host[(size_t)i * feed_len];
+    const int ctl[3] = {n_prompt, feed_len, max_out};
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->tokens, first.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s),
+                  "axdec: tokens upload");
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->pos, zeros.data(), sizeof(int) * M, cudaMemcpyHostToDevice, s),
+                  "axdec: pos reset");
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice, s),
+                  "axdec: ctl upload");
+    // the staging vectors above are pageable host memory: the copies complete
+    // before cudaMemcpyAsync returns, so they may go out of scope
+    return AXQ8_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int axdec_tensor_index(const axdec_config_t* c, const char* name) {
+    if (!c || !name) return -1;
+    if (!strcmp(name, "token_embd.weight")) return 0;
+    if (!strcmp(name, "output.weight")) return 1;
+    if (!strcmp(name, "output_norm.weight")) return 2;
+    int layer;
+    std::string slot;
+    if (!parse_layer_name(name, &layer, &slot) || layer < 0 || layer >= c->n_layers) return -1;
+    const int si = slot_index(slot);
+    return si < 0 ? -1 : 3 + 9 * layer + si;
+}
+
+int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
+    if (!cfg || !out) return fail(AXQ8_ERR_INVALID, "axdec_create: null argument");
+    const axdec_config_t c = *cfg;
+    if (c.n_layers <= 0 || c.hidden <= 0 || c.ffn <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
+        c.vocab <= 0 || c.max_batch <= 0 || c.max_ctx <= 0)
+        return fail(AXQ8_ERR_INVALID, "axdec_create: non-positive dimension");
+    if (c.hidden % QK || c.ffn % QK || c.n_heads % c.n_kv_heads ||
+        c.n_heads * c.head_dim % QK)
+        return fail(AXQ8_ERR_INVALID, "axdec_create: dimensions must be multiples of 32 and "
+                                      "n_heads a multiple of n_kv_heads");
+    if (c.head_dim != 32 && c.head_dim != 64 && c.head_dim != 128)
+        return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: head_dim %d (32, 64, 128 supported)",
+                    c.head_dim);
+    if (c.kv_block != 16) return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: kv_block must be 16");
+    if (c.n_heads / c.n_kv_heads > 16)
+        return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: more than 16 query heads per kv head");
+    if (c.act_mode != AXQ8_ACT_Q8 && c.act_mode != AXQ8_ACT_F32)
+        return fail(AXQ8_ERR_INVALID, "axdec_create: bad act_mode");
+    DeviceState* ds = device_state();
+    if (!ds) return AXQ8_ERR_CUDA;
+    axdec_model* m = new axdec_model();
+    m->c = c;
+    m->ds = ds;
+    m->Nq = c.n_heads * c.head_dim;
+    m->Nkv = c.n_kv_heads * c.head_dim;
+    m->Nqkv = m->Nq + 2 * m->Nkv;
+    m->rs_h = q8r_row_stride(c.hidden);
+    m->rs_q = q8r_row_stride(m->Nq);
+    m->rs_f = q8r_row_stride(c.ffn);
+    m->max_blocks = (c.max_ctx + c.kv_block - 1) / c.kv_block;
+    // split the context so that attention has ~2 CTAs per SM at full length
+    const int target = (2 * ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
+                       (c.n_kv_heads * c.max_batch);
+    m->nsplit = std::max(1, std::min(target, m->max_blocks));
+    m->bps = (m->max_blocks + m->nsplit - 1) / m->nsplit;
+    m->nsplit = (m->max_blocks + m->bps - 1) / m->bps;
+    int rc = AXQ8_OK;
+    const int M = c.max_batch, H = c.hidden, F = c.ffn;
+    const size_t kvsz = c.kv_fp32 ? 4 : 2;
+    const int64_t pages = (int64_t)M * m->max_blocks;
+    m->embd = (uint8_t*)dalloc(m, (size_t)c.vocab * m->rs_h, &rc);
+    m->out_w = (uint8_t*)dalloc(m, (size_t)c.vocab * m->rs_h, &rc);
+    m->out_norm = (float*)dalloc(m, sizeof(float) * H, &rc);
+    m->L.resize(c.n_layers);
+    for (int l = 0; l < c.n_layers && rc == AXQ8_OK; l++) {
+        Layer& Ly = m->L[l];
+        Ly.qkv = (uint8_t*)dalloc(m, (size_t)m->Nqkv * m->rs_h, &rc);
+        Ly.o = (uint8_t*)dalloc(m, (size_t)H * m->rs_q, &rc);
+        Ly.gu = (uint8_t*)dalloc(m, (size_t)2 * F * m->rs_h, &rc);
+        Ly.down = (uint8_t*)dalloc(m, (size_t)H * m->rs_f, &rc);
+        Ly.attn_norm = (float*)dalloc(m, sizeof(float) * H, &rc);
+        Ly.ffn_norm = (float*)dalloc(m, sizeof(float) * H, &rc);
+        Ly.kc = dalloc(m, (size_t)pages * c.n_kv_heads * c.kv_block * c.head_dim * kvsz, &rc);
+        Ly.vc = dalloc(m, (size_t)pages * c.n_kv_heads * c.kv_block * c.head_dim * kvsz, &rc);
+    }
+    const int maxK = std::max(std::max(H, F), m->Nq);
+    m->h = (float*)dalloc(m, sizeof(float) * M * H, &rc);
+    m->xq = (int8_t*)dalloc(m, (size_t)M * maxK, &rc);
+    m->dx = (float*)dalloc(m, sizeof(float) * M * (maxK / QK), &rc);
+    m->x32 = (float*)dalloc(m, sizeof(float) * M * maxK, &rc);
+    m->qkv = (float*)dalloc(m, sizeof(float) * M * m->Nqkv, &rc);
+    m->gu = (float*)dalloc(m, sizeof(float) * M * 2 * F, &rc);
+    m->part = (float*)dalloc(m, sizeof(float) * (size_t)M * c.n_heads * m->nsplit * (c.head_dim + 2), &rc);
+    m->logits = (float*)dalloc(m, sizeof(float) * (size_t)M * c.vocab, &rc);
+    m->rope = (float2*)dalloc(m, sizeof(float2) * (size_t)c.max_ctx * (c.head_dim / 2), &rc);
+    m->block_table = (int*)dalloc(m, sizeof(int) * pages, &rc);
+    m->tokens = (int*)dalloc(m, sizeof(int) * M, &rc);
+    m->pos = (int*)dalloc(m, sizeof(int) * M, &rc);
+    m->feed = (int*)dalloc(m, sizeof(int) * (size_t)M * c.max_ctx, &rc);
+    m->out_tokens = (int*)dalloc(m, sizeof(int) * (size_t)M * c.max_ctx, &rc);
+    m->argmax = (int*)dalloc(m, sizeof(int) * M, &rc);
+    m->ctl = (int*)dalloc(m, sizeof(int) * 4, &rc);
+    if (rc == AXQ8_OK) {
+        cudaError_t e = cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking);
+        if (e != cudaSuccess) rc = cuda_fail(e, "axdec: stream create");
+    }
+    if (rc == AXQ8_OK) {
+        // RoPE table with the reference's expressions (mha.cpp:38-41), on the host
+        const int half = c.head_dim / 2;
+        std::vector<float2> tab((size_t)c.max_ctx * half);
+        for (int p = 0; p < c.max_ctx; p++)
+            for (int i = 0; i < half; i++) {
+                const float freq = 1.0f / std::pow(c.rope_theta, (float)(2 * i) / (float)c.head_dim);
+                const float angle = (float)p * freq;
+                tab[(size_t)p * half + i] = make_float2(std::cos(angle), std::sin(angle));
+            }
+        // identity page assignment: sequence b owns pages [b*max_blocks, ...)
+        std::vector<int> bt(pages);
+        for (int64_t i = 0; i < pages; i++) bt[i] = (int)i;
+        cudaError_t e = cudaMemcpy(m->rope, tab.data(), sizeof(float2) * tab.size(), cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemcpy(m->block_table, bt.data(), sizeof(int) * pages, cudaMemcpyHostToDevice);
+        if (e == cudaSuccess) e = cudaMemset(m->feed, 0, sizeof(int) * (size_t)M * c.max_ctx);
+        if (e == cudaSuccess) e = cudaMemset(m->tokens, 0, sizeof(int) * M);
+        if (e == cudaSuccess) e = cudaMemset(m->pos, 0, sizeof(int) * M);
+        if (e == cudaSuccess) {
+            const int ctl[4] = {1, 1, 0, 0};
+            e = cudaMemcpy(m->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice);
+        }
+        if (e != cudaSuccess) rc = cuda_fail(e, "axdec: init upload");
+    }
+    if (rc != AXQ8_OK) {
+        axdec_destroy(m);
+        return rc;
+    }
+    *out = m;
+    return AXQ8_OK;
+}
+
+int axdec_destroy(axdec_model_t* m) {
+    if (!m) return AXQ8_OK;
+    for (auto& kv : m->graphs)
+        if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
+    if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
+    for (void* p : m->allocs) cudaFree(p);
+    delete m;
+    return AXQ8_OK;
+}
+
+int64_t axdec_device_bytes(const axdec_model_t* m) { return m ? m->bytes : 0; }
+
+int64_t axdec_weight_bytes_per_step(const axdec_model_t* m) {
+    if (!m) return 0;
+    const axdec_config_t& c = m->c;
+    const int64_t H = c.hidden, F = c.ffn;
+    const int64_t per_layer = (int64_t)m->Nqkv * H + H * m->Nq + 2 * F * H + H * F;
+    const int64_t params = per_layer * c.n_layers + (int64_t)c.vocab * H;   // + LM head
+    return params / QK * Q8_0_BYTES;
+}
+
+int axdec_set_tensor(axdec_model_t* m, const char* name, const void* host, int ggml_type,
+                     int64_t rows, int64_t cols) {
+    if (!m || !name || !host) return fail(AXQ8_ERR_INVALID, "axdec_set_tensor: null argument");
+    Dest d;
+    int rc = resolve(m, name, &d);
+    if (rc) return rc;
+    if (d.f32) {
+        if (ggml_type != 0 || rows * cols != d.n)
+            return fail(AXQ8_ERR_INVALID, "axdec_set_tensor: '%s' must be F32 with %lld values",
+                        name, (long long)d.n);
+        AXQ8_CUDA_TRY(cudaMemcpy(d.f32, host, sizeof(float) * d.n, cudaMemcpyHostToDevice),
+                      "axdec_set_tensor: copy");
+        return AXQ8_OK;
+    }
+    if (ggml_type != 8 || rows != d.N || cols != d.K)
+        return fail(AXQ8_ERR_INVALID,
+                    "axdec_set_tensor: '%s' must be Q8_0 [%lld, %lld] (got type %d [%lld, %lld])",
+                    name, (long long)d.N, (long long)d.K, ggml_type, (long long)rows,
+                    (long long)cols);
+    if (!strcmp(name, "output.weight")) m->out_set = true;
+    const size_t bytes = (size_t)rows * (cols / QK) * Q8_0_BYTES;
+    void* staging = nullptr;
+    AXQ8_CUDA_TRY(cudaMalloc(&staging, bytes), "axdec_set_tensor: staging");
+    cudaError_t e = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        rc = axq8_weight_repack(staging, rows, cols, d.rows + d.row0 * q8r_row_stride(cols), nullptr);
+        if (rc == AXQ8_OK) e = cudaDeviceSynchronize();
+    }
+    cudaFree(staging);
+    if (e != cudaSuccess) return cuda_fail(e, "axdec_set_tensor: upload");
+    if (rc) return rc;
+    if (!m->out_set && !strcmp(name, "token_embd.weight")) {
+        // tied LM head until output.weight arrives
+        AXQ8_CUDA_TRY(cudaMemcpy(m->out_w, m->embd, (size_t)m->c.vocab * m->rs_h,
+                                 cudaMemcpyDeviceToDevice),
+                      "axdec_set_tensor: tie lm head");
+    }
+    return AXQ8_OK;
+}
+
+int axdec_init_random(axdec_model_t* m, uint64_t seed, float stdv) {
+    if (!m) return fail(AXQ8_ERR_INVALID, "axdec_init_random: null model");
+    const axdec_config_t& c = m->c;
+    std::vector<std::string> names = {"token_embd.weight", "output.weight", "output_norm.weight"};
+    for (int l = 0; l < c.n_layers; l++)
+        for (int s = 0; s < 9; s++) names.push_back("blk." + std::to_string(l) + "." + kSlots[s] + ".weight");
+    for (const std::string& n : names) {
+        Dest d;
+        int rc = resolve(m, n.c_str(), &d);
+        if (rc) return rc;
+        if (d.f32) {
+            fill_kernel<<<64, 256>>>(d.f32, d.n, 1.0f);
+            AXQ8_CUDA_TRY(cudaGetLastError(), "axdec_init_random: fill");
+            continue;
+        }
+        const uint64_t sd = seed + (uint64_t)axdec_tensor_index(&c, n.c_str());
+        rc = axq8_synth_q8_0(sd, d.N, d.K, 0.0f, stdv, 1, d.rows + d.row0 * q8r_row_stride(d.K), nullptr);
+        if (rc) return rc;
+    }
+    m->out_set = true;
+    AXQ8_CUDA_TRY(cudaDeviceSynchronize(), "axdec_init_random: synchronize");
+    return AXQ8_OK;
+}
+
+int axdec_generate(axdec_model_t* m, const int32_t* prompts, int32_t n_seq, int32_t n_prompt,
+                   int32_t n_new, int32_t* out_tokens, float* logits_out, float* decode_ms,
+                   void* stream) {
+    if (!m || !prompts || !out_tokens) return fail(AXQ8_ERR_INVALID, "axdec_generate: null argument");
+    if (n_seq <= 0 || n_seq > m->c.max_batch || n_prompt <= 0 || n_new <= 0)
+        return fail(AXQ8_ERR_INVALID, "axdec_generate: bad sizes");
+    if (n_prompt + n_new - 1 > m->c.max_ctx)
+        return fail(AXQ8_ERR_INVALID, "axdec_generate: %d positions exceed max_ctx %d",
+                    n_prompt + n_new - 1, m->c.max_ctx);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaGraphExec_t g;
+    int rc = get_graph(m, n_seq, &g);
+    if (rc) return rc;
+    if ((rc = reset_run(m, prompts, n_seq, n_prompt, n_prompt, n_new, s))) return rc;
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (decode_ms) {
+        AXQ8_CUDA_TRY(cudaEventCreate(&e0), "event");
+        AXQ8_CUDA_TRY(cudaEventCreate(&e1), "event");
+    }
+    const int total = n_prompt - 1 + n_new;
+    const size_t lbytes = sizeof(float) * (size_t)n_seq * m->c.vocab;
+    for (int r = 0; r < total; r++) {
+        if (decode_ms && r == n_prompt - 1) cudaEventRecord(e0, s);
+        AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec: graph launch");
+        if (logits_out && r >= n_prompt - 1) {
+            AXQ8_CUDA_TRY(cudaMemcpyAsync(logits_out + (size_t)(r - n_prompt + 1) * n_seq * m->c.vocab,
+                                          m->logits, lbytes, cudaMemcpyDeviceToHost, s),
+                          "axdec: logits copy");
+        }
+    }
+    if (decode_ms) cudaEventRecord(e1, s);
+    // generated tokens: out_tokens rows of max_out = n_new
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->out_tokens, sizeof(int) * (size_t)n_seq * n_new,
+                                  cudaMemcpyDeviceToHost, s),
+                  "axdec: tokens copy");
+    AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec: generate");
+    if (decode_ms) {
+        cudaEventElapsedTime(decode_ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    return AXQ8_OK;
+}
+
+int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t n_prompt,
+                 int32_t n_steps, float* logits_out, void* stream) {
+    if (!m || !tokens || !logits_out) return fail(AXQ8_ERR_INVALID, "axdec_forced: null argument");
+    if (n_seq <= 0 || n_seq > m->c.max_batch || n_prompt <= 0 || n_steps < n_prompt ||
+        n_steps > m->c.max_ctx)
+        return fail(AXQ8_ERR_INVALID, "axdec_forced: bad sizes");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaGraphExec_t g;
+    int rc = get_graph(m, n_seq, &g);
+    if (rc) return rc;
+    const int n_out = n_steps - n_prompt + 1;
+    if ((rc = reset_run(m, tokens, n_seq, n_steps, n_prompt, n_out, s))) return rc;
+    const size_t lbytes = sizeof(float) * (size_t)n_seq * m->c.vocab;
+    for (int r = 0; r < n_steps; r++) {
+        AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec: graph launch");
+        if (r >= n_prompt - 1)
+            AXQ8_CUDA_TRY(cudaMemcpyAsync(logits_out + (size_t)(r - n_prompt + 1) * n_seq * m->c.vocab,
+                                          m->logits, lbytes, cudaMemcpyDeviceToHost, s),
+                          "axdec: logits copy");
+    }
+    AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec: forced");
+    return AXQ8_OK;
+}
+
+}  // extern "C"

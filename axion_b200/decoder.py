@@ -1,0 +1,138 @@
+"""Llama-architecture greedy decoder over the C ABI of include/axdec.h.
+
+Mirrors the reference's ``ModelRunner`` (inference/cpp/runtime/model_runner.hpp:39-106):
+configuration resolved from GGUF metadata the same way (``resolve_config``,
+model_runner.cpp:22-97), ``generate`` with greedy sampling, plus a
+teacher-forced logits mode for parity tests.  Weights are uploaded once and
+stay on the device.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from dataclasses import dataclass
+
+import numpy as np
+
+from . import _lib
+from ._lib import check
+from .gguf import F32, Q8_0, GGUFLoader
+
+
+@dataclass
+class DecoderConfig:
+    n_layers: int
+    hidden: int
+    ffn: int
+    n_heads: int
+    n_kv_heads: int
+    head_dim: int
+    vocab: int
+    rope_theta: float = 10000.0
+    rms_eps: float = 1e-5
+    max_batch: int = 1
+    max_ctx: int = 512
+    kv_block: int = 16
+    act_mode: str = "q8"         # "q8" (A8, decode default) or "f32" (reference arithmetic)
+    kv_fp32: bool = False        # fp16 KV pages by default
+
+    def c(self) -> _lib.axdec_config_t:
+        return _lib.axdec_config_t(
+            self.n_layers, self.hidden, self.ffn, self.n_heads, self.n_kv_heads, self.head_dim,
+            self.vocab, self.rope_theta, self.rms_eps, self.max_batch, self.max_ctx,
+            self.kv_block, _lib.AXQ8_ACT_Q8 if self.act_mode == "q8" else _lib.AXQ8_ACT_F32,
+            1 if self.kv_fp32 else 0)
+
+
+def config_from_gguf(g: GGUFLoader, **kw) -> DecoderConfig:
+    """resolve_config (model_runner.cpp:22-97) on our loader."""
+    a = g.architecture() or "llama"
+    n_heads = g.get_u32(f"{a}.attention.head_count", 1) or 1
+    hidden = g.get_u32(f"{a}.embedding_length", 0)
+    hd = g.get_u32(f"{a}.rope.dimension_count", 0) or (hidden // n_heads if hidden else 0)
+    vocab = g.get_u32(f"{a}.vocab_size", 0) or g.get_arr_len("tokenizer.ggml.tokens", 0) \
+        or g.tensor_shape("token_embd.weight")[0]
+    ffn = g.get_u32(f"{a}.feed_forward_length", 0) or g.tensor_shape("blk.0.ffn_up.weight")[0]
+    return DecoderConfig(
+        n_layers=g.get_u32(f"{a}.block_count", 0), hidden=hidden, ffn=ffn, n_heads=n_heads,
+        n_kv_heads=g.get_u32(f"{a}.attention.head_count_kv", n_heads), head_dim=hd, vocab=vocab,
+        rope_theta=g.get_f32(f"{a}.rope.freq_base", 10000.0),
+        rms_eps=g.get_f32(f"{a}.attention.layer_norm_rms_epsilon", 1e-6), **kw)
+
+
+class Decoder:
+    def __init__(self, cfg: DecoderConfig):
+        import torch  # noqa: F401  (initialises the CUDA context torch also uses)
+        self.cfg = cfg
+        self.lib = _lib.load()
+        self._cc = cfg.c()
+        h = C.c_void_p()
+        check(self.lib.axdec_create(C.byref(self._cc), C.byref(h)))
+        self.h = h
+
+    def close(self) -> None:
+        if self.h:
+            self.lib.axdec_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    # -- weights ---------------------------------------------------------------
+    @classmethod
+    def from_gguf(cls, path, **kw) -> "Decoder":
+        g = GGUFLoader()
+        g.load_file(path)
+        d = cls(config_from_gguf(g, **kw))
+        for name in g.tensor_names():
+            info = g.tensor_info(name)
+            if info.type not in (Q8_0, F32):
+                raise RuntimeError(f"{name}: GGUF type {info.type} not supported (Q8_0/F32)")
+            raw = np.ascontiguousarray(g.load_tensor_raw(name))
+            rows, cols = (info.shape if len(info.shape) == 2 else (1, info.shape[0]))
+            check(d.lib.axdec_set_tensor(d.h, name.encode(), raw.ctypes.data_as(C.c_void_p),
+                                         info.type, rows, cols))
+        return d
+
+    def init_random(self, seed: int, std: float = 0.02) -> None:
+        check(self.lib.axdec_init_random(self.h, seed, std))
+
+    def tensor_index(self, name: str) -> int:
+        return self.lib.axdec_tensor_index(C.byref(self._cc), name.encode())
+
+    @property
+    def device_bytes(self) -> int:
+        return self.lib.axdec_device_bytes(self.h)
+
+    @property
+    def weight_bytes_per_step(self) -> int:
+        return self.lib.axdec_weight_bytes_per_step(self.h)
+
+    # -- decoding --------------------------------------------------------------
+    def generate(self, prompts, n_new: int, logits: bool = False, stream=None):
+        """Greedy continuation of prompts [n_seq, n_prompt] (or one prompt).
+        Returns (tokens [n_seq, n_new], logits [n_new, n_seq, vocab] | None,
+        decode_ms of the n_new generation steps)."""
+        p = np.ascontiguousarray(np.atleast_2d(np.asarray(prompts, np.int32)))
+        n_seq, n_prompt = p.shape
+        out = np.empty((n_seq, n_new), np.int32)
+        lg = np.empty((n_new, n_seq, self.cfg.vocab), np.float32) if logits else None
+        ms = C.c_float(0)
+        check(self.lib.axdec_generate(
+            self.h, p.ctypes.data_as(C.c_void_p), n_seq, n_prompt, n_new,
+            out.ctypes.data_as(C.c_void_p),
+            lg.ctypes.data_as(C.c_void_p) if lg is not None else None, C.byref(ms),
+            C.c_void_p(stream) if stream else None))
+        return out, lg, ms.value
+
+    def forced(self, tokens, n_prompt: int, stream=None) -> np.ndarray:
+        """Teacher-forced logits [n_steps - n_prompt + 1, n_seq, vocab]."""
+        t = np.ascontiguousarray(np.atleast_2d(np.asarray(tokens, np.int32)))
+        n_seq, n_steps = t.shape
+        lg = np.empty((n_steps - n_prompt + 1, n_seq, self.cfg.vocab), np.float32)
+        check(self.lib.axdec_forced(self.h, t.ctypes.data_as(C.c_void_p), n_seq, n_prompt,
+                                    n_steps, lg.ctypes.data_as(C.c_void_p),
+                                    C.c_void_p(stream) if stream else None))
+        return lg

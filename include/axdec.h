@@ -1,0 +1,101 @@
+/*
+ * axdec.h — C ABI of the B200 decode step built on the Q8_0 linear path.
+ *
+ * A Llama-architecture decoder (RMSNorm, GQA attention with NEOX RoPE over a
+ * paged KV cache, SwiGLU FFN, LM head) whose every linear is the Q8_0 GEMV of
+ * axq8.h.  It replaces, for Q8_0 GGUF models (paths inside the reference):
+ *   StreamingExecutor::begin_decode / decode_step / decode_layer
+ *       inference/cpp/runtime/streaming_executor.hpp:58-67, .cpp:244-420
+ *   ModelRunner::generate (greedy)            inference/cpp/runtime/model_runner.cpp:245-317
+ *   mha_attention_incremental + append_row    inference/cpp/runtime/mha.cpp:227-285,
+ *                                             streaming_executor.cpp:255-266
+ *   PagedKVCache (fp32 pages)                 inference/cpp/runtime/paged_kv.hpp:18-41
+ * Weights are uploaded once and stay resident; the KV cache is paged
+ * (fixed-size blocks of tokens, per-sequence block tables); one decode step
+ * for a batch of sequences is a CUDA graph of fused kernels.
+ *
+ * Same conventions as axq8.h: plain C, status codes, axq8_last_error().
+ */
+#ifndef AXION_B200_AXDEC_H
+#define AXION_B200_AXDEC_H
+
+#include <stdint.h>
+
+#include "axq8_status.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct axdec_config {
+    int32_t n_layers;     /* <arch>.block_count */
+    int32_t hidden;       /* <arch>.embedding_length */
+    int32_t ffn;          /* <arch>.feed_forward_length */
+    int32_t n_heads;      /* <arch>.attention.head_count */
+    int32_t n_kv_heads;   /* <arch>.attention.head_count_kv */
+    int32_t head_dim;     /* <arch>.rope.dimension_count (hidden / n_heads) */
+    int32_t vocab;
+    float rope_theta;     /* <arch>.rope.freq_base */
+    float rms_eps;        /* <arch>.attention.layer_norm_rms_epsilon */
+    int32_t max_batch;    /* sequences decoded together */
+    int32_t max_ctx;      /* tokens per sequence (prompt + generated) */
+    int32_t kv_block;     /* tokens per KV page, power of two (16) */
+    int32_t act_mode;     /* AXQ8_ACT_Q8 (decode default) or AXQ8_ACT_F32 */
+    int32_t kv_fp32;      /* 0: fp16 KV pages (default), 1: fp32 pages */
+} axdec_config_t;
+
+typedef struct axdec_model axdec_model_t;
+
+/* Create a model on the current device and allocate its weights, KV pages and
+ * activation buffers (the only allocations; none happen per step). */
+int axdec_create(const axdec_config_t* cfg, axdec_model_t** out);
+int axdec_destroy(axdec_model_t* m);
+
+/* Set one tensor by its GGUF name (token_embd.weight, blk.N.attn_q.weight,
+ * ..., output_norm.weight, output.weight) from host memory: Q8_0 blocks
+ * (ggml_type 8) for the linears and the embedding, F32 (ggml_type 0) for the
+ * norm weights.  rows x cols is the row-major shape ([out, in]).  When
+ * output.weight is never set the LM head is tied to token_embd.weight
+ * (select_output_weight_name, model_runner.cpp:179-189). */
+int axdec_set_tensor(axdec_model_t* m, const char* name, const void* host_data, int ggml_type,
+                     int64_t rows, int64_t cols);
+
+/* Random-init every weight on the device: each Q8_0 tensor from
+ * axq8_synth_q8_0(seed + axdec_tensor_index(name), std), norm weights 1.0. */
+int axdec_init_random(axdec_model_t* m, uint64_t seed, float std);
+
+/* Canonical index of a tensor name (the per-tensor seed offset above), or -1:
+ * token_embd 0, output 1, output_norm 2, then per layer i: 3 + 9*i + slot
+ * with slots attn_norm, attn_q, attn_k, attn_v, attn_output, ffn_norm,
+ * ffn_gate, ffn_up, ffn_down. */
+int axdec_tensor_index(const axdec_config_t* cfg, const char* name);
+
+/* Greedy generation for n_seq sequences (<= max_batch) sharing one prompt
+ * length: prompts[n_seq, n_prompt] (host), then n_new greedy tokens written
+ * to out_tokens[n_seq, n_new] (host).  The prompt is fed one position at a
+ * time through the decode step, as ModelRunner::generate does.  When
+ * logits_out is non-null it receives the LM-head logits of every generated
+ * step [n_new, n_seq, vocab] (host; slows the loop: one copy per step).
+ * The decode step runs as a CUDA graph on `stream`.  On return *decode_ms
+ * (nullable) holds the device time of the n_new generation steps alone. */
+int axdec_generate(axdec_model_t* m, const int32_t* prompts, int32_t n_seq, int32_t n_prompt,
+                   int32_t n_new, int32_t* out_tokens, float* logits_out, float* decode_ms,
+                   void* stream);
+
+/* Teacher-forced variant: feeds tokens[n_seq, n_steps] (prompt followed by
+ * forced continuations) and returns, for every position p >= n_prompt - 1,
+ * the logits of the next token: logits_out[n_steps - n_prompt + 1, n_seq, vocab]. */
+int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t n_prompt,
+                 int32_t n_steps, float* logits_out, void* stream);
+
+/* Bytes of device memory the model holds (weights + KV pages + buffers). */
+int64_t axdec_device_bytes(const axdec_model_t* m);
+
+/* Bytes of Q8_0 weight streamed by one decode step (all linears + LM head,
+ * at 34 bytes per 32 weights) — the algorithmic weight traffic per token. */
+int64_t axdec_weight_bytes_per_step(const axdec_model_t* m);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* AXION_B200_AXDEC_H */

@@ -44,7 +44,7 @@ from oracle.oracle import Oracle, RefLib  # noqa: E402
 SEED = 0xA710
 
 # tiny Llama-architecture model (shapes chosen so every linear is Q8_0-legal)
-TINY = dict(n_layers=2, hidden=64, n_heads=4, n_kv_heads=2, head_dim=16, ffn=128, vocab=96,
+TINY = dict(n_layers=2, hidden=128, n_heads=4, n_kv_heads=2, head_dim=32, ffn=256, vocab=96,
             rope_theta=10000.0, rms_eps=1e-5)
 TINY_PROMPT = [5, 17, 3, 88, 42, 9]
 TINY_NEW = 12

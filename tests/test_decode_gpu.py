@@ -1,0 +1,211 @@
+"""Parity of the device decode step (include/axdec.h) with the reference and the oracle.
+
+* A32 mode + fp32 KV pages: greedy tokens equal the reference's
+  ModelRunner::generate on tests/golden/tiny_llama.gguf, and every step's
+  logits are within a relative 1e-3 (of the step's largest |logit|) of the
+  reference's.
+* A8 mode + fp16 KV pages (the decode default): against the oracle's decode
+  with the same conventions (oracle/model.py act="q8", kv="f16"), free
+  running and teacher forced: first step within 1e-3, later steps within
+  A8_TOL (see below), greedy tokens consistent with the oracle's margins.
+* Batches of different prompts equal independent single-sequence runs.
+* Long contexts (many KV pages, many attention splits).
+* TinyLlama architecture at full size (22 layers, 2048/5632, 32/4 heads,
+  vocab 32000) with device-generated weights against the oracle.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+REL_TOL = 1e-3
+# A8 mode is discontinuous: a last-bit fp32 difference in a reduction (tree on
+# the device, sequential in the oracle) can move one activation across a
+# rounding boundary, i.e. by a whole quantization step (1/127 of its block
+# maximum), and the difference then persists in the KV cache.  Steps after
+# the first are therefore held to A8_TOL, and greedy tokens must agree
+# wherever the oracle's top-2 margin exceeds that tolerance.
+A8_TOL = 5e-2
+
+
+def _rel(a: np.ndarray, b: np.ndarray) -> float:
+    """max |a - b| / max |b| per step (rows of the leading axis)."""
+    a = a.reshape(a.shape[0], -1).astype(np.float64)
+    b = b.reshape(b.shape[0], -1).astype(np.float64)
+    return float(np.max(np.max(np.abs(a - b), axis=1) / np.max(np.abs(b), axis=1)))
+
+
+def _top1_consistent(lg: np.ndarray, ref: np.ndarray, tol: float) -> bool:
+    """Per step: same argmax, or the two candidates are within tol of each other
+    in the reference logits (relative to the step's largest |logit|)."""
+    for a, r in zip(lg.reshape(lg.shape[0], -1), ref.reshape(ref.shape[0], -1)):
+        ia, ir = int(np.argmax(a)), int(np.argmax(r))
+        if ia != ir and abs(r[ia] - r[ir]) > tol * np.max(np.abs(r)):
+            return False
+    return True
+
+
+def _decoder(cuda, **kw):
+    from axion_b200.decoder import Decoder
+    return Decoder.from_gguf(golden("tiny_llama.gguf"), **kw)
+
+
+def test_generate_f32_matches_reference(cuda):
+    ref = golden("tiny_llama_ref.npz")
+    prompt = ref["prompt"]
+    n_new = len(ref["tokens"]) - len(prompt)
+    d = _decoder(cuda, act_mode="f32", kv_fp32=True, max_ctx=32)
+    toks, lg, ms = d.generate(prompt, n_new, logits=True)
+    assert toks[0].tolist() == ref["tokens"][len(prompt):].tolist()
+    assert _rel(lg[:, 0, :], ref["logits"]) <= REL_TOL
+    d.close()
+
+
+def test_generate_f32_fp16_pages_matches_oracle(cuda, oracle):
+    """fp16 KV pages round K and V (relative 2^-11): compared with the oracle
+    holding the same fp16 cache, not with the reference's fp32 cache."""
+    from oracle.model import OracleLlama
+    ref = golden("tiny_llama_ref.npz")
+    prompt = ref["prompt"].tolist()
+    om = OracleLlama.from_gguf(golden("tiny_llama.gguf"), oracle)
+    o_logits, o_toks = om.decode(prompt, 12, act="f32", kv="f16")
+    d = _decoder(cuda, act_mode="f32", kv_fp32=False, max_ctx=32)
+    toks, lg, _ = d.generate(prompt, 12, logits=True)
+    assert toks[0].tolist() == o_toks
+    assert _rel(lg[:, 0, :], o_logits) <= REL_TOL
+    d.close()
+
+
+def test_forced_f32_matches_reference(cuda):
+    ref = golden("tiny_llama_ref.npz")
+    d = _decoder(cuda, act_mode="f32", kv_fp32=True, max_ctx=32)
+    toks = ref["tokens"][:-1]                # prompt + generated, last one not fed
+    lg = d.forced(toks, len(ref["prompt"]))
+    assert _rel(lg[:, 0, :], ref["logits"]) <= REL_TOL
+    d.close()
+
+
+def test_generate_q8_matches_oracle(cuda, oracle):
+    from oracle.model import OracleLlama
+    ref = golden("tiny_llama_ref.npz")
+    prompt = ref["prompt"].tolist()
+    n_new = 12
+    om = OracleLlama.from_gguf(golden("tiny_llama.gguf"), oracle)
+    o_logits, o_toks = om.decode(prompt, n_new, act="q8", kv="f16")
+    d = _decoder(cuda, act_mode="q8", kv_fp32=False, max_ctx=32)
+    toks, lg, _ = d.generate(prompt, n_new, logits=True)
+    assert _rel(lg[:1, 0, :], o_logits[:1]) <= REL_TOL
+    assert _rel(lg[:, 0, :], o_logits) <= A8_TOL
+    assert _top1_consistent(lg[:, 0, :], o_logits, A8_TOL)
+    forced = d.forced(prompt + o_toks[:-1], len(prompt))
+    assert _rel(forced[:1, 0, :], o_logits[:1]) <= REL_TOL
+    assert _rel(forced[:, 0, :], o_logits) <= A8_TOL
+    assert _top1_consistent(forced[:, 0, :], o_logits, A8_TOL)
+    d.close()
+
+
+def test_batch_equals_single_sequences(cuda):
+    rng = np.random.default_rng(3)
+    prompts = rng.integers(0, 96, (3, 7)).astype(np.int32)
+    d = _decoder(cuda, act_mode="q8", max_batch=3, max_ctx=32)
+    batch, blg, _ = d.generate(prompts, 8, logits=True)
+    d1 = _decoder(cuda, act_mode="q8", max_batch=1, max_ctx=32)
+    for i in range(3):
+        one, olg, _ = d1.generate(prompts[i:i + 1], 8, logits=True)
+        assert one[0].tolist() == batch[i].tolist()
+        assert _rel(blg[:, i, :], olg[:, 0, :]) <= 1e-5
+    d.close(), d1.close()
+
+
+def test_long_context_matches_oracle(cuda, oracle):
+    """150-token prompt: ~10 KV pages, every attention split in use."""
+    from oracle.model import OracleLlama
+    rng = np.random.default_rng(9)
+    prompt = rng.integers(0, 96, 150).tolist()
+    om = OracleLlama.from_gguf(golden("tiny_llama.gguf"), oracle)
+    o_logits, o_toks = om.decode(prompt, 4, act="f32", kv="f32")
+    d = _decoder(cuda, act_mode="f32", kv_fp32=True, max_ctx=160)
+    toks, lg, _ = d.generate(prompt, 4, logits=True)
+    assert toks[0].tolist() == o_toks
+    assert _rel(lg[:, 0, :], o_logits) <= REL_TOL
+    d.close()
+
+
+def test_tied_lm_head_and_bad_token(cuda):
+    """No output.weight: the LM head is token_embd (model_runner.cpp tie rule);
+    an out-of-range prompt token is reported through the status word."""
+    from axion_b200 import ops
+    from axion_b200.decoder import Decoder, DecoderConfig
+    cfg = DecoderConfig(n_layers=1, hidden=128, ffn=256, n_heads=4, n_kv_heads=2, head_dim=32,
+                        vocab=64, max_ctx=16)
+    d = Decoder(cfg)
+    d.init_random(5, std=0.2)
+    toks, _, _ = d.generate([1, 2, 3], 2)
+    assert toks.shape == (1, 2) and (0 <= toks).all() and (toks < 64).all()
+    ops.status_clear()
+    d.generate([1, 200, 3], 1)
+    assert ops.status() != 0
+    ops.status_clear()
+    d.close()
+
+
+def _tinyllama_cfg(**kw):
+    from axion_b200.decoder import DecoderConfig
+    return DecoderConfig(n_layers=22, hidden=2048, ffn=5632, n_heads=32, n_kv_heads=4,
+                         head_dim=64, vocab=32000, rope_theta=10000.0, rms_eps=1e-5, **kw)
+
+
+def test_tinyllama_architecture_full_size_vs_oracle(cuda, oracle):
+    """Config 2 architecture with device-generated weights: the oracle (which
+    regenerates the same weights bit for bit) agrees on logits and tokens."""
+    from axion_b200.decoder import Decoder
+    from oracle.model import LlamaConfig, OracleLlama
+    cfg = _tinyllama_cfg(max_ctx=64)
+    d = Decoder(cfg)
+    seed = 0xA710
+    d.init_random(seed, std=0.02)
+    prompt = [11, 2049, 31000, 7]
+    toks, lg, _ = d.generate(prompt, 3, logits=True)
+    t = {}
+    names = ["token_embd.weight", "output.weight"]
+    for i in range(cfg.n_layers):
+        names += [f"blk.{i}.{s}.weight" for s in
+                  ("attn_q", "attn_k", "attn_v", "attn_output", "ffn_gate", "ffn_up", "ffn_down")]
+    shapes = {"attn_q": (2048, 2048), "attn_k": (256, 2048), "attn_v": (256, 2048),
+              "attn_output": (2048, 2048), "ffn_gate": (5632, 2048), "ffn_up": (5632, 2048),
+              "ffn_down": (2048, 5632)}
+    for n in names:
+        N, K = (32000, 2048) if not n.startswith("blk.") else shapes[n.split(".")[2]]
+        t[n] = ("q8", oracle.synth_q8_0(seed + d.tensor_index(n), N, K, 0.02), N, K)
+    ones = np.ones(2048, np.float32)
+    t["output_norm.weight"] = ("f32", ones)
+    for i in range(cfg.n_layers):
+        t[f"blk.{i}.attn_norm.weight"] = ("f32", ones)
+        t[f"blk.{i}.ffn_norm.weight"] = ("f32", ones)
+    om = OracleLlama(LlamaConfig(22, 2048, 32, 4, 64, 5632, 32000, 10000.0, 1e-5), t, oracle)
+    o_logits, o_toks = om.decode(prompt, 3, act="q8", kv="f16")
+    err = _rel(lg[:, 0, :], o_logits)
+    print(f"tinyllama-arch A8 logits rel err vs oracle: {err:.2e}")
+    assert err <= A8_TOL
+    assert _top1_consistent(lg[:, 0, :], o_logits, A8_TOL)
+    d.close()
+
+
+def test_tinyllama_full_workload_runs(cuda):
+    """The benchmark workload shape: 128-token prompt, 256 greedy steps,
+    max_ctx 384; deterministic across runs, no device wait gave up."""
+    from axion_b200 import ops
+    from axion_b200.decoder import Decoder
+    d = Decoder(_tinyllama_cfg(max_ctx=384))
+    d.init_random(0xA710, std=0.02)
+    prompt = np.random.default_rng(0).integers(0, 32000, 128)
+    a, _, ms_a = d.generate(prompt, 256)
+    b, _, ms_b = d.generate(prompt, 256)
+    assert np.array_equal(a, b)
+    assert ms_a > 0 and ms_b > 0
+    assert ops.status() == 0
+    d.close()
