@@ -2,9 +2,21 @@
 """Benchmark of the B200 Q8_0 hot path; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl axion|reference]
-                    [--workload gemv]
+                    [--workload decode|gemv]
 
 Workloads
+  decode (default) TinyLlama-1.1B-architecture decode: 22
+         layers, hidden 2048, FFN 5632 SwiGLU, 32 query / 4 KV heads of 64,
+         vocab 32000, random-init Q8_0 weights (N(0, 0.02) before
+         quantization, generated on the device), batch 1, a random 128-token
+         prompt, then K (default 256) greedy decode steps over paged fp16 KV
+         (block 16).  One step = one decode token.  Metric: decode tokens/s
+         (device time of the K generation steps).  `e2e`: the same tokens over
+         the whole public axdec_generate call (host prompt in, host tokens
+         out, the 128 prompt positions included).  `roofline`: the step as a
+         weight stream (Q8_0 weights of all linears + LM head + KV read per
+         step) against the measured HBM bandwidth.  The reference arm runs
+         ModelRunner::generate on a GGUF holding the same weights.
   gemv   Q8_0 GEMV, TinyLlama ffn_up shape: W [5632 x 2048] Q8_0 (random init,
          N(0, 0.02) before quantization), x [1 x 2048] fp32 N(0, 1) quantized on
          the fly, y [5632] fp32.  One step = one linear_from_gguf call.  The
@@ -355,7 +367,173 @@ def gemv_reference(args, steps: int) -> dict:
 
 # ---------------------------------------------------------------------------
 
-WORKLOADS = {"gemv": (run_gemv_axion, gemv_reference)}
+# ---------------------------------------------------------------------------
+# TinyLlama-architecture decode workload
+# ---------------------------------------------------------------------------
+
+TL = dict(n_layers=22, hidden=2048, ffn=5632, n_heads=32, n_kv_heads=4, head_dim=64,
+          vocab=32000, rope_theta=10000.0, rms_eps=1e-5)
+TL_PROMPT, TL_NEW, TL_SEED, TL_STD = 128, 256, 0xA710, 0.02
+DECODE_METRIC = "TinyLlama-arch Q8_0 decode tokens/s (batch 1, 128-token prompt, greedy)"
+DECODE_CONFIG = {"workload": "tinyllama_1.1b_arch_decode_q8_0", "layers": 22, "hidden": 2048,
+                 "ffn": 5632, "heads": "32q/4kv x 64", "vocab": 32000, "batch": 1,
+                 "prompt": TL_PROMPT, "new_tokens": TL_NEW, "kv": "paged fp16, block 16",
+                 "act": "q8 (A8W8 int8 block dots)",
+                 "l2_policy": "weights 1.1 GB per step >> L2 (126 MB)"}
+
+
+def tl_prompt(rank: int = 0):
+    import numpy as np
+    return np.random.default_rng(1234 + rank).integers(0, TL["vocab"], TL_PROMPT).astype("int32")
+
+
+def tl_kv_bytes(ctx: int) -> int:
+    """K and V bytes one step reads at context length ctx (fp16 pages)."""
+    return TL["n_layers"] * 2 * ctx * TL["n_kv_heads"] * TL["head_dim"] * 2
+
+
+def run_decode_axion(args, d: Dist) -> dict:
+    import torch
+    from axion_b200 import ops
+    from axion_b200.decoder import Decoder, DecoderConfig
+    dev = torch.device("cuda", d.local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    K_new = args.steps
+    cfg = DecoderConfig(**TL, max_batch=1, max_ctx=TL_PROMPT + max(K_new, args.warmup),
+                        act_mode="q8")
+    dec = Decoder(cfg)
+    dec.init_random(TL_SEED, TL_STD)
+    prompt = tl_prompt(d.rank)
+    sp = stream.cuda_stream
+    # warm-up: builds and instantiates the step graph, runs W decode steps
+    dec.generate(prompt, args.warmup, stream=sp)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device_uuid(dev), period_ms=10).start()
+    time.sleep(0.15)
+    d.barrier()
+    torch.cuda.synchronize()
+    # timed: K greedy decode steps (device events inside axdec_generate)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    toks, _, decode_ms = dec.generate(prompt, K_new, stream=sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    d.barrier()
+    clk = clocks.stop()
+    call_ms = e0.elapsed_time(e1)          # the whole public call, host prompt in/tokens out
+    ms_max = d.max(decode_ms)
+    e2e_ms = d.max(call_ms)
+    n_tok = d.sum(K_new) if d.world > 1 else K_new
+    value = n_tok / (ms_max / 1e3)
+    e2e_val = n_tok / (e2e_ms / 1e3)
+    # roofline: the decode step is a weight stream; algorithmic bytes per step
+    # = Q8_0 weights (34/32 B per weight, all linears + LM head) + KV read
+    wbytes = dec.weight_bytes_per_step
+    mean_kv = sum(tl_kv_bytes(TL_PROMPT + i) for i in range(K_new)) / K_new
+    step_ms = ms_max / K_new
+    achieved = (wbytes + mean_kv) / (step_ms / 1e3) / 1e9
+    peaks, peak_kind = measured_peaks()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": ncu_traffic(DECODE_CONFIG["workload"]),
+                "kernel": "decode step (q8_gemv_kernel dominant)", "step_us": round(step_ms * 1e3, 2),
+                "algorithmic_bytes_per_step": int(wbytes + mean_kv), "peak_source": peak_kind}
+    status = ops.status()
+    dev_bytes = dec.device_bytes
+    dec.close()
+    return {
+        "metric": DECODE_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": d.world,
+        "steps": K_new, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32 -> fp32 (A8W8), fp16 KV",
+        "data": "synthetic (device-generated Q8_0 weights N(0,0.02), norms 1.0; "
+                "random prompt token ids)",
+        "config": dict(DECODE_CONFIG, parallelism=f"replicas x{d.world}",
+                       device_bytes=dev_bytes),
+        "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": round(TL_PROMPT * 4 / K_new, 3),
+                "d2h_bytes_per_step": 4,
+                "path": "axdec_generate (C ABI): host prompt in, host tokens out, "
+                        "prompt positions included"},
+        "roofline": roofline,
+        "gpu_launches": (1 + 10 * TL["n_layers"] + 3) * K_new,
+        "clocks": clk,
+        "device_status": status,
+        "first_tokens": [int(t) for t in toks[0][:8]],
+    }
+
+
+def decode_reference(args, steps: int) -> dict:
+    """ModelRunner::generate of the reference on a GGUF with the same weights
+    (the oracle's generator reproduces the device weights bit for bit), on the
+    host cores.  Bounded sample: a short prompt + `steps` new tokens; every
+    position costs one decode_step (the reference prefills token by token),
+    so the rate is positions processed per second."""
+    import ctypes as C
+    import numpy as np
+    from axion_b200 import _lib
+    from axion_b200.decoder import DecoderConfig
+    from axion_b200.gguf import F32, Q8_0, GGUFWriter
+    from oracle.oracle import Oracle, RefLib
+    o, r = Oracle(), RefLib()
+    lib = _lib.load()
+    cc = DecoderConfig(**TL, max_ctx=TL_PROMPT + TL_NEW).c()
+    H, F, V = TL["hidden"], TL["ffn"], TL["vocab"]
+    hq = TL["n_heads"] * TL["head_dim"]
+    hkv = TL["n_kv_heads"] * TL["head_dim"]
+    g = GGUFWriter()
+    g.add_string("general.architecture", "llama")
+    for k, v in [("block_count", TL["n_layers"]), ("attention.head_count", TL["n_heads"]),
+                 ("attention.head_count_kv", TL["n_kv_heads"]), ("embedding_length", H),
+                 ("feed_forward_length", F), ("rope.dimension_count", TL["head_dim"]),
+                 ("vocab_size", V)]:
+        g.add_u32(f"llama.{k}", v)
+    g.add_f32("llama.rope.freq_base", TL["rope_theta"])
+    g.add_f32("llama.attention.layer_norm_rms_epsilon", TL["rms_eps"])
+
+    def q8(name, N, K):
+        seed = TL_SEED + lib.axdec_tensor_index(C.byref(cc), name.encode())
+        g.add_tensor(name, o.synth_q8_0(seed, N, K, TL_STD), (N, K), Q8_0)
+
+    ones = np.ones(H, np.float32)
+    q8("token_embd.weight", V, H)
+    for i in range(TL["n_layers"]):
+        p = f"blk.{i}."
+        g.add_tensor(p + "attn_norm.weight", ones, (H,), F32)
+        q8(p + "attn_q.weight", hq, H)
+        q8(p + "attn_k.weight", hkv, H)
+        q8(p + "attn_v.weight", hkv, H)
+        q8(p + "attn_output.weight", H, hq)
+        g.add_tensor(p + "ffn_norm.weight", ones, (H,), F32)
+        q8(p + "ffn_gate.weight", F, H)
+        q8(p + "ffn_up.weight", F, H)
+        q8(p + "ffn_down.weight", H, F)
+    g.add_tensor("output_norm.weight", ones, (H,), F32)
+    q8("output.weight", V, H)
+    tmp = Path(tempfile.mkdtemp()) / "tinyllama_arch_q8_0.gguf"
+    g.write(tmp)
+    del g
+    prompt = tl_prompt(0)[:2]
+    sec, toks = r.time_generate(tmp, prompt, steps)
+    tmp.unlink()
+    positions = len(prompt) + steps
+    return {"value": round(positions / sec, 4), "unit": "tokens/s", "cores": host_cores(),
+            "kind": "reference",
+            "sample": f"ModelRunner::generate, {len(prompt)}-token prompt + {steps} new tokens "
+                      f"({positions} decode_step calls, each re-reading and dequantizing the "
+                      f"1.1 GB of Q8_0 weights), OpenMP threads={host_cores()}",
+            "seconds": round(sec, 3), "steps": positions}
+
+
+WORKLOADS = {
+    # name: (axion arm, reference/cpu-baseline arm, metric, config, default K, reference sample)
+    "decode": (run_decode_axion, decode_reference, DECODE_METRIC, DECODE_CONFIG, TL_NEW, 3),
+    "gemv": (run_gemv_axion, gemv_reference, "Q8_0 GEMV HBM GB/s (algorithmic bytes)",
+             {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K, "M": 1},
+             200000, 300),
+}
 
 
 def main() -> int:
@@ -364,28 +542,28 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["axion", "reference"], default="axion")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="gemv")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
     ap.add_argument("--cpu-sample", type=int, default=None,
-                    help="reference calls timed for cpu_baseline")
+                    help="size of the reference sample timed for cpu_baseline")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    run_axion, run_ref = WORKLOADS[args.workload]
+    run_axion, run_ref, metric, config, k_default, sample_default = WORKLOADS[args.workload]
     d = Dist(args.gpus)
 
     if args.impl == "reference":
         if d.rank != 0:
             return 0
-        steps = args.steps or 30
-        cb = run_ref(args, steps)
-        out = {"impl": "reference", "metric": "Q8_0 GEMV HBM GB/s (algorithmic bytes)",
-               "value": cb["value"], "unit": cb["unit"], "n_gpus": args.gpus, "steps": steps,
-               "warmup": args.warmup, "ms_per_step": round(cb["seconds"] * 1e3 / steps, 3),
+        sample = args.cpu_sample or sample_default
+        cb = run_ref(args, sample)
+        steps = cb.get("steps", sample)
+        out = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"],
+               "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
+               "ms_per_step": round(cb["seconds"] * 1e3 / steps, 3),
                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
-               "dtype": "fp32 (reference dequantizes Q8_0 to fp32)",
-               "data": "synthetic (host-generated Q8_0 GGUF, same recipe)",
-               "config": {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K,
-                          "M": 1, "parallelism": "host OpenMP"},
+               "dtype": "fp32 (the reference dequantizes Q8_0 to fp32)",
+               "data": "synthetic (host-generated Q8_0 GGUF, same weights as the axion arm)",
+               "config": dict(config, parallelism=f"host OpenMP x{cb['cores']}"),
                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                        "d2h_bytes_per_step": 0}}
@@ -393,14 +571,13 @@ def main() -> int:
         return 0
 
     if args.steps is None:
-        args.steps = 200000
+        args.steps = k_default
     d.init("nccl")
     res = run_axion(args, d)
     if d.rank == 0:
-        sample = args.cpu_sample or 300
         try:
-            res["cpu_baseline"] = {k: v for k, v in run_ref(args, sample).items()
-                                   if k != "seconds"}
+            cb = run_ref(args, args.cpu_sample or sample_default)
+            res["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         except Exception as e:  # the reference library did not travel / build
             res["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
         print(json.dumps(res))
