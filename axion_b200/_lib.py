@@ -74,6 +74,7 @@ SIGNATURES: dict[str, tuple] = {
     "axdec_forced": (_I32, [_P, _P, _I32, _I32, _I32, _P, _P]),
     "axdec_device_bytes": (_I64, [_P]),
     "axdec_weight_bytes_per_step": (_I64, [_P]),
+    "axdec_step_kernels": (_I32, [_P, _I32]),
     "axq8_status_read": (_I32, [C.POINTER(C.c_int)]),
     "axq8_status_clear": (_I32, []),
     "axq8_last_error": (C.c_char_p, []),

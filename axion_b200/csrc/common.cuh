@@ -105,6 +105,14 @@ __device__ inline void bulk_g2s(void* smem_dst, const void* gmem_src, uint32_t b
         : "memory");
 }
 
+// ---- cp.async (16 bytes global -> shared, no register staging) -------------
+__device__ inline void cp_async16(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gmem_src)
+                 : "memory");
+}
+__device__ inline void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // ---- programmatic dependent launch ----------------------------------------
 // wait: block until the preceding grid in the stream has completed and its
 // writes are visible (no-op when the launch had no programmatic edge).

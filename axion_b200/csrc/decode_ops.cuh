@@ -4,15 +4,13 @@
 //   token_embedding           inference/cpp/runtime/token_embedding.cpp (row of the
 //                             dequantized token_embd, gguf.cpp:870-882)
 //   rmsnorm                   inference/cpp/kernels/rmsnorm.cpp:12-100
-//   rope_apply_row_at (NEOX)  inference/cpp/runtime/mha.cpp:15-55, :200-225
-//   append_row                inference/cpp/runtime/streaming_executor.cpp:255-266
 //   mha_attention_incremental inference/cpp/runtime/mha.cpp:227-285
 //   silu * up                 inference/cpp/kernels/silu.cpp:13-65, elementwise.cpp:13-67
-//   greedy argmax             inference/cpp/runtime/sampler.cpp:11-24
 //
 // Every kernel calls griddepcontrol.wait before its first global write or
 // its first read of data another kernel produced, and every kernel of the
-// step does so unconditionally: completion of kernel i then implies
+// step (these and the GEMVs of q8_gemv.cuh, whose RoPE/KV-append and argmax
+// epilogues also live there) does so unconditionally: completion of kernel i then implies
 // completion of all earlier kernels, which is what makes programmatic
 // dependent launch safe for the reuse of activation buffers across phases.
 // A8 producers (Q8 = true) quantize their output in 32-blocks with the
@@ -26,22 +24,9 @@
 
 #include "axq8.h"
 #include "common.cuh"
+#include "q8_gemv.cuh"
 
 namespace axq8 {
-
-__device__ inline float kv_to_float(__half v) { return __half2float(v); }
-__device__ inline float kv_to_float(float v) { return v; }
-__device__ inline void kv_store(__half* p, float v) { *p = __float2half_rn(v); }
-__device__ inline void kv_store(float* p, float v) { *p = v; }
-
-// Quantize one 32-block held one element per lane (all 32 lanes active).
-__device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, float* d) {
-    const uint32_t abits = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
-    const float amax = __uint_as_float(abits);
-    const float id = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
-    q[lane] = (int8_t)q8_round(__fmul_rn(v, id));
-    if (lane == 0) *d = __fdiv_rn(amax, 127.0f);
-}
 
 // ---- embedding ----------------------------------------------------------------
 // h[m, :] = dequantized row tokens[m] of token_embd (repacked Q8_0 rows).
@@ -101,136 +86,135 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     }
 }
 
-// ---- RoPE (NEOX) + KV page append ----------------------------------------------
-// One CTA per sequence.  qkv row = [q (n_heads*hd) | k (n_kv*hd) | v (n_kv*hd)].
-// The rotation uses the host-computed table tab[pos][i] = (cos, sin) of
-// pos * theta^(-2i/hd), evaluated with the same expressions as the
-// reference, and rounds a*c - b*s / a*s + b*c like its scalar code.  Rotated
-// k and v are stored in the layer's pages: page = block_table[m][pos / B],
-// layout [page][n_kv][B][hd].
-template <typename KV>
-__global__ void rope_kv_kernel(float* __restrict__ qkv, int ldq, const int* __restrict__ pos,
-                               const float2* __restrict__ tab, int max_ctx, int n_heads, int n_kv,
-                               int hd, KV* __restrict__ kc, KV* __restrict__ vc,
-                               const int* __restrict__ block_table, int max_blocks, int B,
-                               int* status) {
-    pdl_launch_dependents();
-    pdl_wait();
-    const int m = blockIdx.x;
-    const int p = pos[m];
-    if (p < 0 || p >= max_ctx) {
-        if (threadIdx.x == 0) record_status(status, AXQ8_ERR_INVALID);
-        return;
-    }
-    const int half = hd / 2;
-    float* row = qkv + (int64_t)m * ldq;
-    const float2* t = tab + (int64_t)p * half;
-    const int page = block_table[m * max_blocks + p / B];
-    const int slot = p % B;
-    const int nq_pairs = n_heads * half;
-    const int nk_pairs = n_kv * half;
-    for (int i = threadIdx.x; i < nq_pairs + nk_pairs; i += blockDim.x) {
-        const bool is_k = i >= nq_pairs;
-        const int ii = is_k ? i - nq_pairs : i;
-        const int head = ii / half, j = ii % half;
-        float* base = row + (is_k ? n_heads * hd : 0) + head * hd;
-        const float a = base[j], b = base[j + half];
-        const float2 cs = t[j];
-        const float r0 = __fsub_rn(__fmul_rn(a, cs.x), __fmul_rn(b, cs.y));
-        const float r1 = __fadd_rn(__fmul_rn(a, cs.y), __fmul_rn(b, cs.x));
-        if (!is_k) {
-            base[j] = r0;
-            base[j + half] = r1;
-        } else {
-            KV* dst = kc + (((int64_t)page * n_kv + head) * B + slot) * hd;
-            kv_store(dst + j, r0);
-            kv_store(dst + j + half, r1);
-        }
-    }
-    const float* v = row + (n_heads + n_kv) * hd;
-    for (int i = threadIdx.x; i < n_kv * hd; i += blockDim.x) {
-        const int head = i / hd, d = i % hd;
-        kv_store(vc + (((int64_t)page * n_kv + head) * B + slot) * hd + d, v[i]);
-    }
-}
-
 // ---- attention: split-K flash decode ----------------------------------------------
 // Grid (n_kv, M, nsplit); G warps per CTA, warp g serving query head
 // kvh*G + g (GQA: query head h reads kv head h / G, mha.cpp:253-254).  Split
 // s covers KV pages [s*bps, (s+1)*bps) of the sequence's pages in use
-// (ctx = pos + 1 tokens).  Each page (B = 16 tokens) is staged in shared
-// memory as fp32 and shared by the G warps.  Lane l scores token l & 15 over
-// half the head dims (l >> 4); scores are scaled by 1/sqrt(hd) after the
-// dot, as the reference does.  Online softmax; the partial
-// (acc[hd], running max, running sum) of each (sequence, query head, split)
-// goes to `part` and attn_combine_kernel merges the splits.
+// (ctx = pos + 1 tokens).  Up to `cp` pages (B = 16 tokens each) of K and V
+// are copied to shared memory at once with cp.async, in the cache's own
+// type, and shared by the G warps.  Lane l scores token l & 15 over half the
+// head dims (l >> 4), walking the dims from a lane-dependent start so that
+// the 32 lanes hit 32 different banks; scores are scaled by 1/sqrt(hd) after
+// the dot, as the reference does.  Online softmax; the partial (acc[hd],
+// running max, running sum) of each (sequence, query head, split) goes to
+// `part`, and the last split CTA to finish merges them (and, with Q8,
+// quantizes the head's output for the O projection).
+__device__ __forceinline__ float2 kv_pair(const __half* p) {
+    return __half22float2(*reinterpret_cast<const __half2*>(p));
+}
+__device__ __forceinline__ float2 kv_pair(const float* p) {
+    return *reinterpret_cast<const float2*>(p);
+}
+
+// Shared memory of attn_decode_kernel: K and V stages, the G query rows and
+// the split's page ids.
 template <typename KV, int HD>
-__global__ void attn_partial_kernel(const float* __restrict__ qkv, int ldq,
-                                    const int* __restrict__ pos, const KV* __restrict__ kc,
-                                    const KV* __restrict__ vc, const int* __restrict__ block_table,
-                                    int max_blocks, int n_heads, int n_kv, int bps, float scale,
-                                    float* __restrict__ part) {
+inline size_t attn_smem_bytes(int G, int cp, int bps) {
+    return (size_t)2 * cp * 16 * HD * sizeof(KV) + (size_t)G * HD * sizeof(float) +
+           ((size_t)bps * sizeof(int) + 15) / 16 * 16;
+}
+
+template <typename KV, int HD, bool Q8>
+__global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
+                                   const int* __restrict__ pos, const KV* __restrict__ kc,
+                                   const KV* __restrict__ vc, const int* __restrict__ block_table,
+                                   int max_blocks, int n_heads, int n_kv, int bps, int cp,
+                                   float scale, float* __restrict__ part, int* __restrict__ counters,
+                                   float* __restrict__ out, int8_t* __restrict__ xq,
+                                   float* __restrict__ dx) {
     constexpr int B = 16;
     constexpr int DL = HD / 32;            // dims per lane in the value accumulation
-    extern __shared__ __align__(16) float sm[];
+    constexpr int V16 = 16 / sizeof(KV);    // cache elements per 16-byte copy
+    static_assert(HD % 32 == 0 && (DL == 1 || DL % 2 == 0), "head dim");
+    extern __shared__ __align__(16) uint8_t attn_sm[];
     const int G = blockDim.x >> 5;
-    float* ks = sm;                         // [B][HD]
-    float* vs = ks + B * HD;                // [B][HD]
-    float* qs = vs + B * HD;                // [G][HD]
-    pdl_launch_dependents();
-    pdl_wait();
+    KV* ks = reinterpret_cast<KV*>(attn_sm);              // [cp][B][HD]
+    KV* vs = ks + (size_t)cp * B * HD;                     // [cp][B][HD]
+    float* qs = reinterpret_cast<float*>(vs + (size_t)cp * B * HD);   // [G][HD]
+    int* pg = reinterpret_cast<int*>(qs + G * HD);         // [bps] page ids
     const int kvh = blockIdx.x, m = blockIdx.y, s = blockIdx.z, nsplit = gridDim.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int h = kvh * G + warp;
-    // a position past the page table was already reported by rope_kv_kernel;
+    const int b0 = s * bps;
+    // the page table is written by the host before the step: read it while
+    // the previous kernel drains
+    for (int i = threadIdx.x; i < bps; i += blockDim.x)
+        pg[i] = b0 + i < max_blocks ? block_table[m * max_blocks + b0 + i] : 0;
+    pdl_launch_dependents();
+    pdl_wait();
+    // a position past the page table was already reported by the KV append;
     // never read beyond the table
     const int ctx = min(pos[m] + 1, max_blocks * B);
     const int nblk = (ctx + B - 1) / B;
-    const int b0 = s * bps, b1 = min(nblk, b0 + bps);
-    for (int i = threadIdx.x; i < G * HD; i += blockDim.x)
-        qs[i] = qkv[(int64_t)m * ldq + (int64_t)(kvh * G) * HD + i];
+    const int b1 = min(nblk, b0 + bps);
+    for (int i = threadIdx.x; i < G * HD / 4; i += blockDim.x)
+        cp_async16(qs + 4 * i, qkv + (int64_t)m * ldq + (int64_t)(kvh * G) * HD + 4 * i);
     float mrun = -CUDART_INF_F, lrun = 0.0f;
     float acc[DL];
 #pragma unroll
     for (int i = 0; i < DL; i++) acc[i] = 0.0f;
     const int t = lane & (B - 1), hf = lane >> 4;
-    for (int blk = b0; blk < b1; blk++) {
-        __syncthreads();   // previous page fully consumed (and qs written)
-        const int page = block_table[m * max_blocks + blk];
-        const KV* kp = kc + ((int64_t)page * n_kv + kvh) * B * HD;
-        const KV* vp = vc + ((int64_t)page * n_kv + kvh) * B * HD;
-        for (int i = threadIdx.x; i < B * HD; i += blockDim.x) {
-            ks[i] = kv_to_float(kp[i]);
-            vs[i] = kv_to_float(vp[i]);
+    constexpr int per_page = B * HD / V16;
+    for (int c0 = b0; c0 < b1; c0 += cp) {
+        const int np = min(cp, b1 - c0);
+        __syncthreads();   // previous chunk consumed; pg visible
+        for (int i = threadIdx.x; i < np * per_page; i += blockDim.x) {
+            const int p = i / per_page, j = i - p * per_page;
+            const int64_t off = ((int64_t)pg[c0 - b0 + p] * n_kv + kvh) * B * HD + j * V16;
+            cp_async16(ks + p * B * HD + j * V16, kc + off);
+            cp_async16(vs + p * B * HD + j * V16, vc + off);
         }
+        cp_async_wait_all();
         __syncthreads();
-        // score of token t, half hf of the dims, then combine the halves
-        const float* q = qs + warp * HD + hf * (HD / 2);
-        const float* k = ks + t * HD + hf * (HD / 2);
-        float dot = 0.0f;
+        for (int p = 0; p < np; p++) {
+            const int blk = c0 + p;
+            // score of token t, half hf of the dims, then combine the halves
+            const float* q = qs + warp * HD + hf * (HD / 2);
+            const KV* k = ks + ((size_t)p * B + t) * HD + hf * (HD / 2);
+            float dot = 0.0f;
 #pragma unroll 8
-        for (int d = 0; d < HD / 2; d++) dot = fmaf(q[d], k[d], dot);
-        dot += __shfl_xor_sync(0xffffffffu, dot, 16);
-        const bool valid = blk * B + t < ctx;
-        const float sc = valid ? __fmul_rn(dot, scale) : -CUDART_INF_F;
-        float mt = sc;
+            for (int d2 = 0; d2 < HD / 4; d2++) {
+                const int dd = 2 * ((d2 + lane) & (HD / 4 - 1));
+                const float2 kf = kv_pair(k + dd);
+                const float2 qf = *reinterpret_cast<const float2*>(q + dd);
+                dot = fmaf(qf.x, kf.x, dot);
+                dot = fmaf(qf.y, kf.y, dot);
+            }
+            dot += __shfl_xor_sync(0xffffffffu, dot, 16);
+            const bool valid = blk * B + t < ctx;
+            const float sc = valid ? __fmul_rn(dot, scale) : -CUDART_INF_F;
+            float mt = sc;
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
-        const float mnew = fmaxf(mrun, mt);
-        const float corr = expf(mrun - mnew);   // 0 when mrun is -inf
-        const float pt = valid ? expf(sc - mnew) : 0.0f;
-        float ps = pt;
+            for (int o = 8; o > 0; o >>= 1) mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, o));
+            const float mnew = fmaxf(mrun, mt);
+            const float corr = expf(mrun - mnew);   // 0 when mrun is -inf
+            const float pt = valid ? expf(sc - mnew) : 0.0f;
+            float ps = pt;
 #pragma unroll
-        for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
-        lrun = fmaf(lrun, corr, ps);
+            for (int o = 8; o > 0; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+            lrun = fmaf(lrun, corr, ps);
 #pragma unroll
-        for (int i = 0; i < DL; i++) acc[i] *= corr;
-        for (int tt = 0; tt < B; tt++) {
-            const float p = __shfl_sync(0xffffffffu, pt, tt);
+            for (int i = 0; i < DL; i++) acc[i] *= corr;
+            const KV* v = vs + (size_t)p * B * HD + lane * DL;
+#pragma unroll 4
+            for (int tt = 0; tt < B; tt++) {
+                const float pv = __shfl_sync(0xffffffffu, pt, tt);
+                if (DL == 1) {
+                    acc[0] = fmaf(pv, kv_to_float(v[tt * HD]), acc[0]);
+                } else {
 #pragma unroll
-            for (int i = 0; i < DL; i++) acc[i] = fmaf(p, vs[tt * HD + lane * DL + i], acc[i]);
+                    for (int i = 0; i < DL; i += 2) {
+                        const float2 vf = kv_pair(v + tt * HD + i);
+                        acc[i] = fmaf(pv, vf.x, acc[i]);
+                        acc[i + 1] = fmaf(pv, vf.y, acc[i + 1]);
+                    }
+                }
+            }
+            mrun = mnew;
         }
-        mrun = mnew;
+    }
+    if (b0 >= b1) {   // empty split: qs copies still in flight
+        cp_async_wait_all();
     }
     float* o = part + (((int64_t)m * n_heads + h) * nsplit + s) * (HD + 2);
 #pragma unroll
@@ -239,56 +223,57 @@ __global__ void attn_partial_kernel(const float* __restrict__ qkv, int ldq,
         o[HD] = mrun;
         o[HD + 1] = lrun;
     }
-}
-
-// Merge the nsplit partials of each (sequence, query head): one warp each.
-// out = sum_s acc_s * e^(m_s - M) / sum_s l_s * e^(m_s - M).  With Q8 the
-// head's output is quantized in 32-dim blocks (groups of 32/DL lanes).
-template <int HD, bool Q8>
-__global__ void attn_combine_kernel(const float* __restrict__ part, int M, int n_heads, int nsplit,
-                                    float* __restrict__ out, int8_t* __restrict__ xq,
-                                    float* __restrict__ dx) {
-    constexpr int DL = HD / 32;
-    pdl_launch_dependents();
-    pdl_wait();
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
-    const int lane = threadIdx.x & 31;
-    if (gw >= M * n_heads) return;
-    const int m = gw / n_heads, h = gw % n_heads;
-    const float* p = part + ((int64_t)m * n_heads + h) * nsplit * (HD + 2);
-    float mx = -CUDART_INF_F;
-    for (int s = 0; s < nsplit; s++) mx = fmaxf(mx, p[s * (HD + 2) + HD]);
-    float l = 0.0f;
-    float acc[DL];
+    // The last CTA of this (sequence, kv head) merges the splits of its G
+    // query heads (fence, count, fence; counters return to zero):
+    // out = sum_s acc_s e^(m_s - M) / sum_s l_s e^(m_s - M).
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) {
+        int* c = counters + m * n_kv + kvh;
+        last = atomicAdd(c, 1) == nsplit - 1;
+        if (last) *c = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    // one lane per split (nsplit <= 32): every partial is loaded at once
+    const float* ph = part + ((int64_t)m * n_heads + h) * nsplit * (HD + 2);
+    const float ms = lane < nsplit ? __ldcg(ph + lane * (HD + 2) + HD) : -CUDART_INF_F;
+    const float ls = lane < nsplit ? __ldcg(ph + lane * (HD + 2) + HD + 1) : 0.0f;
+    float mx = ms;
 #pragma unroll
-    for (int i = 0; i < DL; i++) acc[i] = 0.0f;
-    for (int s = 0; s < nsplit; s++) {
-        const float ms = p[s * (HD + 2) + HD];
-        if (ms == -CUDART_INF_F) continue;      // empty split
-        const float f = expf(ms - mx);
-        l = fmaf(p[s * (HD + 2) + HD + 1], f, l);
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float f = ms == -CUDART_INF_F ? 0.0f : expf(ms - mx);   // empty splits weigh 0
+    const float l = warp_sum(ls * f);
+    float sum[DL];
 #pragma unroll
-        for (int i = 0; i < DL; i++) acc[i] = fmaf(p[s * (HD + 2) + lane * DL + i], f, acc[i]);
+    for (int i = 0; i < DL; i++) sum[i] = 0.0f;
+#pragma unroll 4
+    for (int t2 = 0; t2 < nsplit; t2++) {
+        const float ft = __shfl_sync(0xffffffffu, f, t2);
+#pragma unroll
+        for (int i = 0; i < DL; i++) sum[i] = fmaf(__ldcg(ph + t2 * (HD + 2) + lane * DL + i), ft, sum[i]);
     }
     const int64_t base = (int64_t)m * n_heads * HD + (int64_t)h * HD + lane * DL;
     float v[DL];
 #pragma unroll
-    for (int i = 0; i < DL; i++) v[i] = __fdiv_rn(acc[i], l);
+    for (int i = 0; i < DL; i++) v[i] = __fdiv_rn(sum[i], l);
     if (!Q8) {
 #pragma unroll
         for (int i = 0; i < DL; i++) out[base + i] = v[i];
         return;
     }
-    // 32-dim block = 32/DL consecutive lanes
-    float a = 0.0f;
+    // 32-dim quantization block = 32/DL consecutive lanes
+    float am = 0.0f;
 #pragma unroll
-    for (int i = 0; i < DL; i++) a = fmaxf(a, fabsf(v[i]));
+    for (int i = 0; i < DL; i++) am = fmaxf(am, fabsf(v[i]));
 #pragma unroll
-    for (int o = 1; o < 32 / DL; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
-    const float id = a == 0.0f ? 0.0f : __fdiv_rn(127.0f, a);
+    for (int off = 1; off < 32 / DL; off <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    const float id = am == 0.0f ? 0.0f : __fdiv_rn(127.0f, am);
 #pragma unroll
     for (int i = 0; i < DL; i++) xq[base + i] = (int8_t)q8_round(__fmul_rn(v[i], id));
-    if ((lane % (32 / DL)) == 0) dx[base / QK] = __fdiv_rn(a, 127.0f);
+    if ((lane % (32 / DL)) == 0) dx[base / QK] = __fdiv_rn(am, 127.0f);
 }
 
 // ---- SiLU(gate) * up (+ A8 quantization) -------------------------------------------
@@ -313,50 +298,6 @@ __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
         out[(int64_t)m * F + i] = a;
     } else {
         quant_block_warp(a, lane, xq + (int64_t)m * F + b * QK, dx + (int64_t)m * nb + b);
-    }
-}
-
-// ---- greedy argmax + advance ----------------------------------------------------------
-// One CTA per sequence.  next = first index of the maximum logit.  Then the
-// next input is the fed token when one remains (prompt / teacher forcing),
-// else `next`; generated tokens are recorded; pos advances by one.
-// ctl = {n_prompt, feed_len, max_out}.
-__global__ void argmax_advance_kernel(const float* __restrict__ logits, int V,
-                                      int* __restrict__ tokens, int* __restrict__ pos,
-                                      const int* __restrict__ feed, const int* __restrict__ ctl,
-                                      int* __restrict__ out_tokens, int* __restrict__ argmax_out) {
-    __shared__ float bv[32];
-    __shared__ int bi[32];
-    pdl_launch_dependents();
-    pdl_wait();
-    const int m = blockIdx.x;
-    const float* lg = logits + (int64_t)m * V;
-    float best = -CUDART_INF_F;
-    int idx = 0x7fffffff;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = lg[i];
-        if (v > best) { best = v; idx = i; }   // ascending i: keeps the first maximum
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, idx, o);
-        if (ov > best || (ov == best && oi < idx)) { best = ov; idx = oi; }
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-    if (lane == 0) { bv[warp] = best; bi[warp] = idx; }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        for (int w = 1; w < nw; w++)
-            if (bv[w] > best || (bv[w] == best && bi[w] < idx)) { best = bv[w]; idx = bi[w]; }
-        if (idx == 0x7fffffff) idx = 0;            // all logits NaN/-inf
-        const int n_prompt = ctl[0], feed_len = ctl[1], max_out = ctl[2];
-        const int p = pos[m];
-        const int np = p + 1;
-        argmax_out[m] = idx;
-        if (np >= n_prompt && np - n_prompt < max_out) out_tokens[m * max_out + (np - n_prompt)] = idx;
-        tokens[m] = np < feed_len ? feed[m * feed_len + np] : idx;
-        pos[m] = np;
     }
 }
 

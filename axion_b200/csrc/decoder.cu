@@ -1,15 +1,20 @@
 // Llama-architecture decode step on B200 built from the Q8_0 GEMV (C ABI in
 // include/axdec.h).
 //
-// One step processes one position of each of M sequences:
-//   embed -> per layer [ rmsnorm(+q8) -> GEMV qkv -> rope + KV page append
-//   -> split-K attention -> combine(+q8) -> GEMV o (+residual, in place)
-//   -> rmsnorm(+q8) -> GEMV gate|up -> silu*up(+q8) -> GEMV down (+residual) ]
-//   -> rmsnorm(+q8) -> GEMV lm_head -> argmax + advance
-// the order of StreamingExecutor::decode_layer (streaming_executor.cpp:268-401)
-// and ModelRunner::generate (model_runner.cpp:245-317).  Q, K and V share one
-// fused weight (rows of attn_q, attn_k, attn_v stacked) and so do gate and up,
-// so each layer streams its weights in four GEMVs.  All kernels are launched
+// One step processes one position of each of M sequences, in the order of
+// StreamingExecutor::decode_layer (streaming_executor.cpp:268-401) and
+// ModelRunner::generate (model_runner.cpp:245-317).  In A8 mode (M <= 4) a
+// layer is five kernels:
+//   GEMV qkv   [prologue rmsnorm->Q8, epilogue NEOX RoPE + KV page append]
+//   attention  [split-K flash decode, last CTA merges splits -> Q8]
+//   GEMV o     [+ residual, in place]
+//   GEMV gu    [prologue rmsnorm->Q8]
+//   GEMV down  [prologue silu(gate)*up->Q8, + residual]
+// plus embed at the start and GEMV lm_head [prologue rmsnorm->Q8, epilogue
+// argmax + state advance] at the end.  A32 mode and wide batches keep
+// RMSNorm and SiLU*up as producer kernels.  Q, K and V share one stacked
+// weight (the rows of Q and K permuted per head to (j, j + hd/2) pairs for
+// the RoPE epilogue), and so do gate and up.  All kernels are launched
 // with programmatic dependent launch and the whole step is captured once in a
 // CUDA graph per batch size; the control state (positions, input tokens, fed
 // tokens) lives in device memory so the same graph serves every step.
@@ -51,6 +56,7 @@ struct Layer {
 
 struct Graph {
     cudaGraphExec_t exec = nullptr;
+    int kernels = 0;
 };
 
 }  // namespace
@@ -85,6 +91,9 @@ struct axdec_model {
     int* out_tokens = nullptr;    // [M, max_ctx]
     int* argmax = nullptr;        // [M]
     int* ctl = nullptr;           // {n_prompt, feed_len, max_out}
+    unsigned long long* amax_key = nullptr;   // [M] argmax epilogue keys
+    int* done = nullptr;                      // argmax epilogue completion counter
+    int* attn_cnt = nullptr;                  // [M, n_kv] attention split counters
     cudaStream_t cap_stream = nullptr;
     std::map<int, Graph> graphs;  // per batch size
 };
@@ -132,6 +141,7 @@ struct Dest {
     int64_t row0 = 0, N = 0, K = 0;
     float* f32 = nullptr;   // norm weight destination
     int64_t n = 0;
+    bool rope_perm = false; // attn_q / attn_k: rows permuted for the RoPE epilogue
 };
 
 int resolve(axdec_model* m, const char* name, Dest* d) {
@@ -149,8 +159,8 @@ int resolve(axdec_model* m, const char* name, Dest* d) {
     switch (si) {
         case 0: d->f32 = Ly.attn_norm; d->n = H; return 0;
         case 5: d->f32 = Ly.ffn_norm; d->n = H; return 0;
-        case 1: *d = {Ly.qkv, 0, m->Nq, H}; return 0;
-        case 2: *d = {Ly.qkv, m->Nq, m->Nkv, H}; return 0;
+        case 1: *d = {Ly.qkv, 0, m->Nq, H}; d->rope_perm = true; return 0;
+        case 2: *d = {Ly.qkv, m->Nq, m->Nkv, H}; d->rope_perm = true; return 0;
         case 3: *d = {Ly.qkv, m->Nq + m->Nkv, m->Nkv, H}; return 0;
         case 4: *d = {Ly.o, 0, H, m->Nq}; return 0;
         case 6: *d = {Ly.gu, 0, F, H}; return 0;
@@ -166,6 +176,35 @@ __global__ void fill_kernel(float* p, int64_t n, float v) {
         p[i] = v;
 }
 
+// Row permutation of a Q or K weight for the RoPE epilogue: within each head,
+// destination row 2j is source dim j and row 2j+1 is source dim j + hd/2, so
+// one GEMV row pair yields exactly one NEOX rotation pair.
+__global__ void rope_permute_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                         int64_t nrows, int hd, int64_t rs) {
+    const int half = hd / 2;
+    for (int64_t r = blockIdx.x; r < nrows; r += gridDim.x) {
+        const int64_t head = r / hd, pr = r % hd;
+        const int64_t srow = head * hd + ((pr & 1) ? half + pr / 2 : pr / 2);
+        const uint4* s4 = reinterpret_cast<const uint4*>(src + srow * rs);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + r * rs);
+        for (int64_t i = threadIdx.x; i < rs / 16; i += blockDim.x) d4[i] = s4[i];
+    }
+}
+
+// Write repacked rows (device, `tmp`) into the destination, permuting Q/K rows.
+int place_rows(axdec_model* m, const Dest& d, const uint8_t* tmp) {
+    const int64_t rs = q8r_row_stride(d.K);
+    uint8_t* dst = d.rows + d.row0 * rs;
+    if (d.rope_perm) {
+        rope_permute_rows_kernel<<<256, 128>>>(tmp, dst, d.N, m->c.head_dim, rs);
+        AXQ8_CUDA_TRY(cudaGetLastError(), "rope_permute_rows launch");
+    } else {
+        AXQ8_CUDA_TRY(cudaMemcpy(dst, tmp, (size_t)d.N * rs, cudaMemcpyDeviceToDevice), "place rows");
+    }
+    AXQ8_CUDA_TRY(cudaDeviceSynchronize(), "place rows");
+    return AXQ8_OK;
+}
+
 template <typename KV>
 int launch_step_kv(axdec_model* m, int M, cudaStream_t s);
 
@@ -173,8 +212,8 @@ int launch_step(axdec_model* m, int M, cudaStream_t s) {
     return m->c.kv_fp32 ? launch_step_kv<float>(m, M, s) : launch_step_kv<__half>(m, M, s);
 }
 
-int gemv(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M, const float* resid,
-         float* y, cudaStream_t s) {
+GemvArgs gemv_args(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
+                   const float* resid, float* y) {
     GemvArgs a = {};
     a.rows = rows;
     a.N = N;
@@ -188,35 +227,29 @@ int gemv(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M, const
     a.y = y;
     a.ldy = N;
     a.status = m->ds->status;
-    return gemv_launch(m->ds, a, m->c.act_mode == AXQ8_ACT_F32, s);
+    a.eps = m->c.rms_eps;
+    return a;
 }
 
 template <typename KV, int HD>
 int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s) {
     const axdec_config_t& c = m->c;
     const int G = c.n_heads / c.n_kv_heads;
-    const size_t smem = (size_t)(2 * 16 + G) * HD * sizeof(float);
+    // pages staged at once: up to 32 KB of K and V
+    const int cp = std::max(1, std::min(m->bps, (int)(32768 / (2 * 16 * HD * sizeof(KV)))));
+    const size_t smem = attn_smem_bytes<KV, HD>(G, cp, m->bps);
+    if (smem > 48 * 1024)
+        return fail(AXQ8_ERR_UNSUPPORTED, "attention: %zu B of shared memory", smem);
     const float scale = 1.0f / std::sqrt((float)HD);   // mha.cpp:250
     Layer& Ly = m->L[layer];
-    AXQ8_CUDA_TRY(launch_k(attn_partial_kernel<KV, HD>, dim3(c.n_kv_heads, M, m->nsplit),
-                           dim3(G * 32), smem, s, true, (const float*)m->qkv, m->Nqkv,
-                           (const int*)m->pos, (const KV*)Ly.kc, (const KV*)Ly.vc,
-                           (const int*)m->block_table, m->max_blocks, c.n_heads, c.n_kv_heads,
-                           m->bps, scale, m->part),
-                  "attn_partial launch");
-    const int warps = M * c.n_heads;
-    const int nb = (warps + 7) / 8;
-    if (c.act_mode == AXQ8_ACT_F32) {
-        AXQ8_CUDA_TRY(launch_k(attn_combine_kernel<HD, false>, dim3(nb), dim3(256), 0, s, true,
-                               (const float*)m->part, M, c.n_heads, m->nsplit, m->x32,
-                               (int8_t*)nullptr, (float*)nullptr),
-                      "attn_combine launch");
-    } else {
-        AXQ8_CUDA_TRY(launch_k(attn_combine_kernel<HD, true>, dim3(nb), dim3(256), 0, s, true,
-                               (const float*)m->part, M, c.n_heads, m->nsplit, (float*)nullptr,
-                               m->xq, m->dx),
-                      "attn_combine launch");
-    }
+    const bool q8 = c.act_mode != AXQ8_ACT_F32;
+    auto kern = q8 ? attn_decode_kernel<KV, HD, true> : attn_decode_kernel<KV, HD, false>;
+    AXQ8_CUDA_TRY(launch_k(kern, dim3(c.n_kv_heads, M, m->nsplit), dim3(G * 32), smem, s, true,
+                           (const float*)m->qkv, m->Nqkv, (const int*)m->pos, (const KV*)Ly.kc,
+                           (const KV*)Ly.vc, (const int*)m->block_table, m->max_blocks, c.n_heads,
+                           c.n_kv_heads, m->bps, cp, scale, m->part, m->attn_cnt, m->x32, m->xq,
+                           m->dx),
+                  "attention launch");
     return AXQ8_OK;
 }
 
@@ -238,47 +271,106 @@ template <typename KV>
 int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
     const axdec_config_t& c = m->c;
     const int H = c.hidden, F = c.ffn, hd = c.head_dim;
+    const bool a32 = c.act_mode == AXQ8_ACT_F32;
+    // fused producers: A8 and the activations of M rows fit in shared memory
+    const bool fuse = !a32 && gemv_fused_prologue_fits(PRO_RMS, M, H) &&
+                      gemv_fused_prologue_fits(PRO_SILU, M, F);
+    const int plain = a32 ? PRO_F32 : PRO_Q8;
+    DeviceState* ds = m->ds;
     int rc;
     AXQ8_CUDA_TRY(launch_k(embed_kernel, dim3(M), dim3(256), 0, s, true, (const uint8_t*)m->embd,
-                           m->rs_h, H, c.vocab, (const int*)m->tokens, m->h, m->ds->status),
+                           m->rs_h, H, c.vocab, (const int*)m->tokens, m->h, ds->status),
                   "embed launch");
     for (int l = 0; l < c.n_layers; l++) {
         Layer& Ly = m->L[l];
-        if ((rc = launch_rmsnorm(m, M, m->h, Ly.attn_norm, s))) return rc;
-        if ((rc = gemv(m, Ly.qkv, m->Nqkv, H, M, nullptr, m->qkv, s))) return rc;
-        AXQ8_CUDA_TRY(launch_k(rope_kv_kernel<KV>, dim3(M), dim3(256), 0, s, true, m->qkv, m->Nqkv,
-                               (const int*)m->pos, (const float2*)m->rope, c.max_ctx, c.n_heads,
-                               c.n_kv_heads, hd, (KV*)Ly.kc, (KV*)Ly.vc,
-                               (const int*)m->block_table, m->max_blocks, c.kv_block,
-                               m->ds->status),
-                      "rope_kv launch");
+        // Q, K, V (+ RoPE, KV append)
+        GemvArgs a = gemv_args(m, Ly.qkv, m->Nqkv, H, M, nullptr, m->qkv);
+        a.pos = m->pos;
+        a.rope = m->rope;
+        a.max_ctx = c.max_ctx;
+        a.n_heads = c.n_heads;
+        a.n_kv = c.n_kv_heads;
+        a.hd = hd;
+        a.kc = Ly.kc;
+        a.vc = Ly.vc;
+        a.block_table = m->block_table;
+        a.max_blocks = m->max_blocks;
+        a.kv_block = c.kv_block;
+        if (fuse) {
+            a.src = m->h;
+            a.norm_w = Ly.attn_norm;
+            rc = gemv_launch_mt<PRO_RMS, EPI_ROPE_KV, KV>(ds, a, s);
+        } else {
+            if ((rc = launch_rmsnorm(m, M, m->h, Ly.attn_norm, s))) return rc;
+            rc = a32 ? gemv_launch_mt<PRO_F32, EPI_ROPE_KV, KV>(ds, a, s)
+                     : gemv_launch_mt<PRO_Q8, EPI_ROPE_KV, KV>(ds, a, s);
+        }
+        if (rc) return rc;
+        // attention (+ split merge, + Q8 of its output)
         if (hd == 32) rc = launch_attention<KV, 32>(m, M, l, s);
         else if (hd == 64) rc = launch_attention<KV, 64>(m, M, l, s);
         else rc = launch_attention<KV, 128>(m, M, l, s);
         if (rc) return rc;
-        if ((rc = gemv(m, Ly.o, H, m->Nq, M, m->h, m->h, s))) return rc;
-        if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s))) return rc;
-        if ((rc = gemv(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu, s))) return rc;
-        const int nwarps = M * (F / QK);
-        if (c.act_mode == AXQ8_ACT_F32) {
-            AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, dim3((nwarps + 7) / 8), dim3(256), 0, s,
-                                   true, (const float*)m->gu, F, M, m->x32, (int8_t*)nullptr,
-                                   (float*)nullptr),
-                          "silu launch");
+        // O projection + residual
+        a = gemv_args(m, Ly.o, H, m->Nq, M, m->h, m->h);
+        rc = plain == PRO_F32 ? gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s)
+                              : gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, s);
+        if (rc) return rc;
+        // gate | up
+        a = gemv_args(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu);
+        if (fuse) {
+            a.src = m->h;
+            a.norm_w = Ly.ffn_norm;
+            rc = gemv_launch_mt<PRO_RMS, EPI_STORE, float>(ds, a, s);
         } else {
-            AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0, s,
-                                   true, (const float*)m->gu, F, M, (float*)nullptr, m->xq, m->dx),
-                          "silu launch");
+            if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s))) return rc;
+            rc = a32 ? gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s)
+                     : gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, s);
         }
-        if ((rc = gemv(m, Ly.down, H, F, M, m->h, m->h, s))) return rc;
+        if (rc) return rc;
+        // down + residual
+        a = gemv_args(m, Ly.down, H, F, M, m->h, m->h);
+        if (fuse) {
+            a.src = m->gu;
+            rc = gemv_launch_mt<PRO_SILU, EPI_STORE, float>(ds, a, s);
+        } else {
+            const int nwarps = M * (F / QK);
+            if (a32) {
+                AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, dim3((nwarps + 7) / 8), dim3(256), 0,
+                                       s, true, (const float*)m->gu, F, M, m->x32,
+                                       (int8_t*)nullptr, (float*)nullptr),
+                              "silu launch");
+                rc = gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s);
+            } else {
+                AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0,
+                                       s, true, (const float*)m->gu, F, M, (float*)nullptr, m->xq,
+                                       m->dx),
+                              "silu launch");
+                rc = gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, s);
+            }
+        }
+        if (rc) return rc;
     }
-    if ((rc = launch_rmsnorm(m, M, m->h, m->out_norm, s))) return rc;
-    if ((rc = gemv(m, m->out_w, c.vocab, H, M, nullptr, m->logits, s))) return rc;
-    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3(M), dim3(512), 0, s, true,
-                           (const float*)m->logits, c.vocab, m->tokens, m->pos,
-                           (const int*)m->feed, (const int*)m->ctl, m->out_tokens, m->argmax),
-                  "argmax launch");
-    return AXQ8_OK;
+    // final norm + LM head + greedy argmax + advance
+    GemvArgs a = gemv_args(m, m->out_w, c.vocab, H, M, nullptr, m->logits);
+    a.pos = m->pos;
+    a.amax_key = m->amax_key;
+    a.done = m->done;
+    a.tokens = m->tokens;
+    a.feed = m->feed;
+    a.ctl = m->ctl;
+    a.out_tokens = m->out_tokens;
+    a.argmax_out = m->argmax;
+    if (fuse) {
+        a.src = m->h;
+        a.norm_w = m->out_norm;
+        rc = gemv_launch_mt<PRO_RMS, EPI_ARGMAX, float>(ds, a, s);
+    } else {
+        if ((rc = launch_rmsnorm(m, M, m->h, m->out_norm, s))) return rc;
+        rc = a32 ? gemv_launch_mt<PRO_F32, EPI_ARGMAX, float>(ds, a, s)
+                 : gemv_launch_mt<PRO_Q8, EPI_ARGMAX, float>(ds, a, s);
+    }
+    return rc;
 }
 
 // Instantiate (once per batch size) the graph of one decode step.  The first
@@ -305,11 +397,24 @@ int get_graph(axdec_model* m, int M, cudaGraphExec_t* out) {
         return rc;
     }
     if (e != cudaSuccess) return cuda_fail(e, "axdec: end capture");
+    // kernel nodes of the step, reported by axdec_step_kernels
+    size_t n_nodes = 0;
+    int kernels = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n_nodes) == cudaSuccess && n_nodes) {
+        std::vector<cudaGraphNode_t> nodes(n_nodes);
+        if (cudaGraphGetNodes(g, nodes.data(), &n_nodes) == cudaSuccess)
+            for (auto nd : nodes) {
+                cudaGraphNodeType t;
+                if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel)
+                    kernels++;
+            }
+    }
     cudaGraphExec_t exec = nullptr;
     e = cudaGraphInstantiate(&exec, g, 0);
     cudaGraphDestroy(g);
     if (e != cudaSuccess) return cuda_fail(e, "axdec: graph instantiate");
     m->graphs[M].exec = exec;
+    m->graphs[M].kernels = kernels;
     *out = exec;
     return AXQ8_OK;
 }
@@ -382,10 +487,12 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->rs_q = q8r_row_stride(m->Nq);
     m->rs_f = q8r_row_stride(c.ffn);
     m->max_blocks = (c.max_ctx + c.kv_block - 1) / c.kv_block;
-    // split the context so that attention has ~2 CTAs per SM at full length
-    const int target = (2 * ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
+    // split the context so that attention fills about one wave of CTAs at full
+    // length, with at least 2 pages per split and at most 32 splits (the
+    // merge gives one lane to each split)
+    const int target = (ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
                        (c.n_kv_heads * c.max_batch);
-    m->nsplit = std::max(1, std::min(target, m->max_blocks));
+    m->nsplit = std::max(1, std::min(std::min(target, (m->max_blocks + 1) / 2), 32));
     m->bps = (m->max_blocks + m->nsplit - 1) / m->nsplit;
     m->nsplit = (m->max_blocks + m->bps - 1) / m->bps;
     int rc = AXQ8_OK;
@@ -424,6 +531,9 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->out_tokens = (int*)dalloc(m, sizeof(int) * (size_t)M * c.max_ctx, &rc);
     m->argmax = (int*)dalloc(m, sizeof(int) * M, &rc);
     m->ctl = (int*)dalloc(m, sizeof(int) * 4, &rc);
+    m->amax_key = (unsigned long long*)dalloc(m, sizeof(unsigned long long) * M, &rc);
+    m->done = (int*)dalloc(m, sizeof(int), &rc);
+    m->attn_cnt = (int*)dalloc(m, sizeof(int) * M * c.n_kv_heads, &rc);
     if (rc == AXQ8_OK) {
         cudaError_t e = cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) rc = cuda_fail(e, "axdec: stream create");
@@ -446,6 +556,9 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
         if (e == cudaSuccess) e = cudaMemset(m->feed, 0, sizeof(int) * (size_t)M * c.max_ctx);
         if (e == cudaSuccess) e = cudaMemset(m->tokens, 0, sizeof(int) * M);
         if (e == cudaSuccess) e = cudaMemset(m->pos, 0, sizeof(int) * M);
+        if (e == cudaSuccess) e = cudaMemset(m->amax_key, 0, sizeof(unsigned long long) * M);
+        if (e == cudaSuccess) e = cudaMemset(m->done, 0, sizeof(int));
+        if (e == cudaSuccess) e = cudaMemset(m->attn_cnt, 0, sizeof(int) * M * c.n_kv_heads);
         if (e == cudaSuccess) {
             const int ctl[4] = {1, 1, 0, 0};
             e = cudaMemcpy(m->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice);
@@ -471,6 +584,12 @@ int axdec_destroy(axdec_model_t* m) {
 }
 
 int64_t axdec_device_bytes(const axdec_model_t* m) { return m ? m->bytes : 0; }
+
+int axdec_step_kernels(const axdec_model_t* m, int n_seq) {
+    if (!m) return -1;
+    auto it = m->graphs.find(n_seq);
+    return it == m->graphs.end() ? -1 : it->second.kernels;
+}
 
 int64_t axdec_weight_bytes_per_step(const axdec_model_t* m) {
     if (!m) return 0;
@@ -503,13 +622,17 @@ int axdec_set_tensor(axdec_model_t* m, const char* name, const void* host, int g
     if (!strcmp(name, "output.weight")) m->out_set = true;
     const size_t bytes = (size_t)rows * (cols / QK) * Q8_0_BYTES;
     void* staging = nullptr;
+    void* tmp = nullptr;
     AXQ8_CUDA_TRY(cudaMalloc(&staging, bytes), "axdec_set_tensor: staging");
-    cudaError_t e = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
+    cudaError_t e = cudaMalloc(&tmp, (size_t)rows * q8r_row_stride(cols));
+    if (e == cudaSuccess) e = cudaMemcpy(staging, host, bytes, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) {
-        rc = axq8_weight_repack(staging, rows, cols, d.rows + d.row0 * q8r_row_stride(cols), nullptr);
+        rc = axq8_weight_repack(staging, rows, cols, tmp, nullptr);
         if (rc == AXQ8_OK) e = cudaDeviceSynchronize();
+        if (rc == AXQ8_OK && e == cudaSuccess) rc = place_rows(m, d, (const uint8_t*)tmp);
     }
     cudaFree(staging);
+    if (tmp) cudaFree(tmp);
     if (e != cudaSuccess) return cuda_fail(e, "axdec_set_tensor: upload");
     if (rc) return rc;
     if (!m->out_set && !strcmp(name, "token_embd.weight")) {
@@ -537,7 +660,17 @@ int axdec_init_random(axdec_model_t* m, uint64_t seed, float stdv) {
             continue;
         }
         const uint64_t sd = seed + (uint64_t)axdec_tensor_index(&c, n.c_str());
-        rc = axq8_synth_q8_0(sd, d.N, d.K, 0.0f, stdv, 1, d.rows + d.row0 * q8r_row_stride(d.K), nullptr);
+        if (!d.rope_perm) {
+            rc = axq8_synth_q8_0(sd, d.N, d.K, 0.0f, stdv, 1, d.rows + d.row0 * q8r_row_stride(d.K),
+                                 nullptr);
+            if (rc) return rc;
+            continue;
+        }
+        void* tmp = nullptr;
+        AXQ8_CUDA_TRY(cudaMalloc(&tmp, (size_t)d.N * q8r_row_stride(d.K)), "axdec_init_random: tmp");
+        rc = axq8_synth_q8_0(sd, d.N, d.K, 0.0f, stdv, 1, tmp, nullptr);
+        if (rc == AXQ8_OK) rc = place_rows(m, d, (const uint8_t*)tmp);
+        cudaFree(tmp);
         if (rc) return rc;
     }
     m->out_set = true;

@@ -11,21 +11,37 @@
 // needs >= 8 outstanding 16-byte loads per thread at >= 1024 threads per SM
 // for ~7 TB/s; 1-D bulk copies need >= 16 KB per copy, 4 KB copies cap at
 // ~2.6 TB/s).  So:
-//  * two CTAs of 16 warps per SM, each CTA owning a contiguous range of rows;
-//  * each warp reduces TWO rows at a time with kChunks 16-byte loads per row
-//    per lane in flight (non-allocating, read-once);
+//  * two CTAs of 16 warps per SM, each CTA owning a contiguous range of row
+//    PAIRS (rows 2p, 2p+1);
+//  * each warp reduces one row pair at a time with kChunks 16-byte loads per
+//    row per lane in flight (non-allocating, read-once);
 //  * the warp's first loads are issued before griddepcontrol.wait: weights do
 //    not depend on the previous kernel, so under programmatic dependent launch
 //    their HBM latency overlaps the tail of the kernel producing the input;
 //  * when a CTA has fewer row pairs than warps (short N, long K), the K range
 //    of each pair is split over several warps and the partial sums are
-//    reduced through shared memory in a fixed order (SPLIT instantiation);
-//  * in A8 mode the quantized activation and its scales are staged once per
-//    CTA in shared memory.
+//    reduced through shared memory in a fixed order (SPLIT instantiation).
+//
+// Prologues (PRO) produce the activation after the dependency wait:
+//   PRO_Q8    pre-quantized xq/dx (staged in shared memory when it fits);
+//   PRO_F32   fp32 x read from global memory (A32);
+//   PRO_RMS   RMSNorm of src[M,K] by norm_w, quantized to Q8 in shared memory
+//             (every CTA computes the same bytes; replaces a producer kernel);
+//   PRO_SILU  silu(gate)*up of src[M, 2K] quantized to Q8 in shared memory.
+// Epilogues (EPI) consume the two sums of a row pair:
+//   EPI_STORE   y = residual + sum;
+//   EPI_ROPE_KV the rows of Q and K are stored permuted so that a pair is
+//               (dim j, dim j + hd/2) of one head: rotate (NEOX RoPE) and
+//               write q back in natural order / k into the KV pages; v rows
+//               go to the V pages (replaces rope_apply_row_at + append_row);
+//   EPI_ARGMAX  store the logits and reduce the greedy argmax over the grid
+//               (packed atomicMax); the last CTA to finish advances the
+//               decode state (next input token, position, generated token).
 #pragma once
 
-#include <cuda_runtime.h>
 #include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <math_constants.h>
 #include <stdint.h>
 #include <stdlib.h>
 
@@ -35,18 +51,41 @@
 
 namespace axq8 {
 
+enum { PRO_Q8 = 0, PRO_F32 = 1, PRO_RMS = 2, PRO_SILU = 3 };
+enum { EPI_STORE = 0, EPI_ROPE_KV = 1, EPI_ARGMAX = 2 };
+
 struct GemvArgs {
     const uint8_t* rows;      // Q8R rows
     int64_t N, K, row_stride;
     int M;
-    const int8_t* xq;         // A8: [M, K] int8, 16-byte aligned
-    const float* dx;          // A8: [M, K/32]
-    const float* x;           // A32: [M, K] fp32, 16-byte aligned
+    const int8_t* xq;         // PRO_Q8: [M, K] int8, 16-byte aligned
+    const float* dx;          // PRO_Q8: [M, K/32]
+    const float* x;           // PRO_F32: [M, K] fp32, 16-byte aligned
     const float* residual;    // nullable, [M, ldy]
     float* y;                 // [M, ldy]
     int64_t ldy;
     int* status;
     int act_smem;             // bytes of staged activation (0: read from global)
+    // PRO_RMS / PRO_SILU
+    const float* src;         // RMS: [M, K]; SILU: [M, 2K] = [gate | up]
+    const float* norm_w;      // RMS weight [K]
+    float eps;
+    // EPI_ROPE_KV
+    int* pos;                 // [M] (advanced by the EPI_ARGMAX tail)
+    const float2* rope;       // [max_ctx][hd/2] (cos, sin)
+    int max_ctx, n_heads, n_kv, hd;
+    void* kc;                 // [pages][n_kv][B][hd]
+    void* vc;
+    const int* block_table;   // [M][max_blocks]
+    int max_blocks, kv_block;
+    // EPI_ARGMAX
+    unsigned long long* amax_key;  // [M], zero between uses
+    int* done;                     // grid completion counter, zero between uses
+    int* tokens;                   // [M] next input token
+    const int* feed;               // [M][feed_len]
+    const int* ctl;                // {n_prompt, feed_len, max_out}
+    int* out_tokens;               // [M][max_out]
+    int* argmax_out;               // [M]
 };
 
 constexpr int kGemvWarps = 16;                 // warps per CTA
@@ -54,7 +93,7 @@ constexpr int kGemvCtasPerSm = 2;
 constexpr int kChunks = 4;                     // 16-byte loads per row per lane in flight
 constexpr int kGemvActSmemMax = 32 * 1024;     // largest staged activation
 constexpr int kGemvMaxMT = 4;
-constexpr int kPartBytes = kGemvWarps * 2 * kGemvMaxMT * 4;   // split-K partials
+constexpr int kPartBytes = kGemvWarps * 2 * kGemvMaxMT * 4;   // split-K partials / scratch
 
 __device__ inline int4 ldg_stream(const void* p) {
     int4 v;
@@ -86,6 +125,32 @@ __device__ inline float dot16_f32(const int4 w, const float* __restrict__ xa) {
         s = fmaf(v.w, (float)(int8_t)((q >> 24) & 0xff), s);
     }
     return s;
+}
+
+__device__ inline float kv_to_float(__half v) { return __half2float(v); }
+__device__ inline float kv_to_float(float v) { return v; }
+__device__ inline void kv_store(__half* p, float v) { *p = __float2half_rn(v); }
+__device__ inline void kv_store(float* p, float v) { *p = v; }
+
+// Quantize one 32-block held one element per lane (all 32 lanes active),
+// the convention of axq8_quantize_act.
+__device__ __forceinline__ void quant_block_warp(float v, int lane, int8_t* q, float* d) {
+    const uint32_t abits = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
+    const float amax = __uint_as_float(abits);
+    const float id = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+    q[lane] = (int8_t)q8_round(__fmul_rn(v, id));
+    if (lane == 0) *d = __fdiv_rn(amax, 127.0f);
+}
+
+// Orderable 64-bit key of (logit, index): larger logit wins, then the smaller
+// index (the first maximum, as the reference's greedy argmax keeps).
+__device__ inline unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v);
+    u = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+    return ((unsigned long long)u << 32) | (unsigned long long)(0xffffffffu - (uint32_t)idx);
+}
+__device__ inline int argmax_key_index(unsigned long long k) {
+    return (int)(0xffffffffu - (uint32_t)(k & 0xffffffffu));
 }
 
 // The 2 x kChunks weight chunks (and their block scales) a lane holds for one
@@ -168,27 +233,6 @@ __device__ __forceinline__ void pair_compute(const PairLoad& L, const GemvArgs& 
 }
 
 template <int MT>
-__device__ __forceinline__ void pair_store(const GemvArgs& a, int64_t n, bool has_b, int m0,
-                                           int lane, float (&acc)[2][MT]) {
-#pragma unroll
-    for (int r = 0; r < 2; r++)
-#pragma unroll
-        for (int j = 0; j < MT; j++) acc[r][j] = warp_sum(acc[r][j]);
-    if (lane < 2 && (lane == 0 || has_b)) {
-        const int r = lane;
-#pragma unroll
-        for (int j = 0; j < MT; j++) {
-            const int m = m0 + j;
-            if (m < a.M) {
-                float v = acc[r][j];
-                if (a.residual) v += a.residual[(int64_t)m * a.ldy + n + r];
-                a.y[(int64_t)m * a.ldy + n + r] = v;
-            }
-        }
-    }
-}
-
-template <int MT>
 __device__ __forceinline__ void acc_zero(float (&acc)[2][MT]) {
 #pragma unroll
     for (int r = 0; r < 2; r++)
@@ -196,18 +240,207 @@ __device__ __forceinline__ void acc_zero(float (&acc)[2][MT]) {
         for (int j = 0; j < MT; j++) acc[r][j] = 0.0f;
 }
 
-template <int MT, bool A32, bool SPLIT>
+constexpr int kArgmaxMaxM = 64;   // sequences an EPI_ARGMAX launch reduces
+
+// Epilogue of one row pair (rows n, n+1) for activation row m, run by one
+// lane holding both sums.  EPI_ARGMAX folds each stored logit into the CTA's
+// shared key of row m.
+template <int EPI, typename KV>
+__device__ __forceinline__ void epi_pair(const GemvArgs& a, int m, int64_t n, bool has_b,
+                                         float v0, float v1, unsigned long long* keys) {
+    if (EPI == EPI_ROPE_KV) {
+        const int hd = a.hd, half = hd / 2, B = a.kv_block;
+        const int64_t Nq = (int64_t)a.n_heads * hd, Nkv = (int64_t)a.n_kv * hd;
+        const int p = a.pos[m];
+        if (p < 0 || p >= a.max_ctx) {
+            record_status(a.status, AXQ8_ERR_INVALID);
+            return;
+        }
+        const int page = a.block_table[m * a.max_blocks + p / B];
+        const int slot = p % B;
+        if (n < Nq + Nkv) {
+            const bool isk = n >= Nq;
+            const int local = (int)(n - (isk ? Nq : 0));
+            const int head = local / hd, j = (local % hd) >> 1;
+            const float2 cs = a.rope[(int64_t)p * half + j];
+            const float r0 = __fsub_rn(__fmul_rn(v0, cs.x), __fmul_rn(v1, cs.y));
+            const float r1 = __fadd_rn(__fmul_rn(v0, cs.y), __fmul_rn(v1, cs.x));
+            if (!isk) {
+                float* q = a.y + (int64_t)m * a.ldy + (int64_t)head * hd;
+                q[j] = r0;
+                q[j + half] = r1;
+            } else {
+                KV* dst = static_cast<KV*>(a.kc) + (((int64_t)page * a.n_kv + head) * B + slot) * hd;
+                kv_store(dst + j, r0);
+                kv_store(dst + j + half, r1);
+            }
+        } else {
+            const int d0 = (int)(n - Nq - Nkv);
+            const int head = d0 / hd, d = d0 % hd;
+            KV* dst = static_cast<KV*>(a.vc) + (((int64_t)page * a.n_kv + head) * B + slot) * hd + d;
+            kv_store(dst, v0);
+            if (has_b) kv_store(dst + 1, v1);
+        }
+        return;
+    }
+#pragma unroll
+    for (int r = 0; r < 2; r++) {
+        if (r == 1 && !has_b) break;
+        float v = r ? v1 : v0;
+        if (a.residual) v += a.residual[(int64_t)m * a.ldy + n + r];
+        a.y[(int64_t)m * a.ldy + n + r] = v;
+        if (EPI == EPI_ARGMAX) atomicMax(keys + m, argmax_key(v, (int)(n + r)));
+    }
+}
+
+// Fused prologues.  Their inputs are first copied to a shared-memory staging
+// area with cp.async (every 16-byte copy in flight at once, no registers
+// held), then thread t handles 4 consecutive elements at a time; the 8 lanes
+// holding one 32-block quantize it together.
+constexpr int kProMaxK = 8192;                      // largest K of a fused prologue
+constexpr int kProStageMax = 64 * 1024;             // largest staging area
+
+// Quantize the 4 values a lane holds; the block is 8 consecutive lanes.
+__device__ __forceinline__ void quant_quad(const float (&v)[4], int lane, int8_t* q4, float* d) {
+    float a = fmaxf(fmaxf(fabsf(v[0]), fabsf(v[1])), fmaxf(fabsf(v[2]), fabsf(v[3])));
+#pragma unroll
+    for (int o = 1; o < 8; o <<= 1) a = fmaxf(a, __shfl_xor_sync(0xffffffffu, a, o));
+    const float id = a == 0.0f ? 0.0f : __fdiv_rn(127.0f, a);
+    uint32_t packed = 0;
+#pragma unroll
+    for (int i = 0; i < 4; i++)
+        packed |= (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[i], id)) << (8 * i);
+    *reinterpret_cast<uint32_t*>(q4) = packed;
+    if ((lane & 7) == 0) *d = __fdiv_rn(a, 127.0f);
+}
+
+// PRO_RMS: act <- Q8(rmsnorm(src[m,:]) * w): out = (x * (1/sqrt(mean(x^2) +
+// eps))) * w with the reference's separately rounded operations
+// (rmsnorm.cpp:47-96); the sum of squares is a fixed tree.
+// stage: x [M][K] then w [K] (fp32).
+template <int NW>
+__device__ __forceinline__ void prologue_rms(const GemvArgs& a, int8_t* act_q, float* act_d,
+                                             float* red, float* stage) {
+    const int K = (int)a.K, nb = K / QK, M = a.M;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    constexpr int T = NW * 32;
+    float* xs = stage;
+    float* ws = stage + (int64_t)M * K;
+    for (int i = threadIdx.x; i < M * K / 4; i += T) cp_async16(xs + 4 * i, a.src + 4 * i);
+    for (int i = threadIdx.x; i < K / 4; i += T) cp_async16(ws + 4 * i, a.norm_w + 4 * i);
+    cp_async_wait_all();
+    __syncthreads();
+    for (int m = 0; m < M; m++) {
+        const float4* x4 = reinterpret_cast<const float4*>(xs + (int64_t)m * K);
+        float s = 0.0f;
+        for (int q = threadIdx.x; q < K / 4; q += T) {
+            const float4 v = x4[q];
+            s = fmaf(v.x, v.x, s);
+            s = fmaf(v.y, v.y, s);
+            s = fmaf(v.z, v.z, s);
+            s = fmaf(v.w, v.w, s);
+        }
+        s = warp_sum(s);
+        if (lane == 0) red[warp] = s;
+        __syncthreads();
+        float t = lane < NW ? red[lane] : 0.0f;
+        t = warp_sum(t);
+        const float ms = __fdiv_rn(t, (float)K);
+        const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, a.eps)));
+        const float4* w4 = reinterpret_cast<const float4*>(ws);
+        for (int q0 = 0; q0 < K / 4; q0 += T) {      // uniform trip count: the 8-lane groups
+            const int q = q0 + threadIdx.x;          // of a block are whole (K % 32 == 0)
+            if (q < K / 4) {
+                const float4 xv = x4[q], wv = w4[q];
+                const float v[4] = {__fmul_rn(__fmul_rn(xv.x, inv), wv.x),
+                                    __fmul_rn(__fmul_rn(xv.y, inv), wv.y),
+                                    __fmul_rn(__fmul_rn(xv.z, inv), wv.z),
+                                    __fmul_rn(__fmul_rn(xv.w, inv), wv.w)};
+                quant_quad(v, lane, act_q + m * K + 4 * q, act_d + m * nb + q / 8);
+            }
+        }
+        __syncthreads();   // red reused by the next row; act complete
+    }
+}
+
+// PRO_SILU: act <- Q8(silu(gate) * up), a = (g / (1 + e^-g)) * u rounded per
+// op as silu.cpp:53-61 and elementwise.cpp:55-63 do.  stage: src [M][2K].
+template <int NW>
+__device__ __forceinline__ void prologue_silu(const GemvArgs& a, int8_t* act_q, float* act_d,
+                                              float* stage) {
+    const int K = (int)a.K, nb = K / QK, M = a.M;
+    const int lane = threadIdx.x & 31;
+    constexpr int T = NW * 32;
+    for (int i = threadIdx.x; i < M * 2 * K / 4; i += T) cp_async16(stage + 4 * i, a.src + 4 * i);
+    cp_async_wait_all();
+    __syncthreads();
+    for (int m = 0; m < M; m++) {
+        const float4* g4 = reinterpret_cast<const float4*>(stage + (int64_t)m * 2 * K);
+        const float4* u4 = reinterpret_cast<const float4*>(stage + (int64_t)m * 2 * K + K);
+        for (int q0 = 0; q0 < K / 4; q0 += T) {
+            const int q = q0 + threadIdx.x;
+            if (q < K / 4) {
+                const float4 gv = g4[q], uv = u4[q];
+                const float gg[4] = {gv.x, gv.y, gv.z, gv.w};
+                const float uu[4] = {uv.x, uv.y, uv.z, uv.w};
+                float v[4];
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    v[j] = __fmul_rn(__fdiv_rn(gg[j], __fadd_rn(1.0f, expf(-gg[j]))), uu[j]);
+                quant_quad(v, lane, act_q + m * K + 4 * q, act_d + m * nb + q / 8);
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// EPI_ARGMAX tail: grid reduction of the CTA keys by packed atomicMax, and
+// the decode-state advance by the last CTA (the completion counter pattern:
+// fence, count, fence).
+__device__ __forceinline__ void argmax_tail(const GemvArgs& a, const unsigned long long* keys) {
+    __syncthreads();
+    for (int m = threadIdx.x; m < a.M; m += blockDim.x)
+        if (keys[m]) atomicMax(a.amax_key + m, keys[m]);
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) last = atomicAdd(a.done, 1) == (int)gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x == 0) {
+        const int n_prompt = a.ctl[0], feed_len = a.ctl[1], max_out = a.ctl[2];
+        for (int m = 0; m < a.M; m++) {
+            const unsigned long long k = atomicExch(a.amax_key + m, 0ull);
+            const int idx = k == 0ull ? 0 : argmax_key_index(k);
+            const int p = a.pos[m];
+            const int np = p + 1;
+            a.argmax_out[m] = idx;
+            if (np >= n_prompt && np - n_prompt < max_out)
+                a.out_tokens[m * max_out + (np - n_prompt)] = idx;
+            a.tokens[m] = np < feed_len ? a.feed[m * feed_len + np] : idx;
+            a.pos[m] = np;
+        }
+        *a.done = 0;
+    }
+}
+
+template <int MT, int PRO, int EPI, bool SPLIT, typename KV>
 __global__ void __launch_bounds__(kGemvWarps * 32, kGemvCtasPerSm) q8_gemv_kernel(const GemvArgs a) {
+    constexpr bool A32 = PRO == PRO_F32;
     extern __shared__ __align__(128) uint8_t smem[];
     float* part = reinterpret_cast<float*>(smem);   // [kGemvWarps][2][MT] split-K partials
     uint8_t* act = smem + kPartBytes;               // staged activation
+    float* stage = reinterpret_cast<float*>(act + a.act_smem);   // fused-prologue inputs
     const int64_t rs = a.row_stride;
     const int K = (int)a.K;
     const int nchunks = K / 16;
-    const int64_t r0 = a.N * blockIdx.x / gridDim.x;
-    const int64_t r1 = a.N * (blockIdx.x + 1) / gridDim.x;
-    const int nrows = (int)(r1 - r0);
-    const int npairs = (nrows + 1) / 2;
+    const int64_t npt = (a.N + 1) / 2;               // row pairs in the matrix
+    const int64_t p0 = npt * blockIdx.x / gridDim.x;
+    const int64_t p1 = npt * (blockIdx.x + 1) / gridDim.x;
+    const int64_t r0 = 2 * p0;
+    const int nrows = (int)(min(a.N, 2 * p1) - r0);
+    const int npairs = (int)(p1 - p0);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     // Warps per row pair (SPLIT only): a power of two with wpp * npairs <=
@@ -237,17 +470,33 @@ __global__ void __launch_bounds__(kGemvWarps * 32, kGemvCtasPerSm) q8_gemv_kerne
 
     const int8_t* xq = a.xq;
     const float* dx = a.dx;
-    if (!A32 && a.act_smem > 0) {
+    {
         int8_t* act_q = reinterpret_cast<int8_t*>(act);
         float* act_d = reinterpret_cast<float*>(act + ((int64_t)a.M * K + 15) / 16 * 16);
-        const int qbytes = a.M * K;
-        for (int o = threadIdx.x * 16; o < qbytes; o += kGemvWarps * 32 * 16)
-            *reinterpret_cast<int4*>(act_q + o) = __ldg(reinterpret_cast<const int4*>(a.xq + o));
-        const int nd = a.M * (K / QK);
-        for (int o = threadIdx.x; o < nd; o += kGemvWarps * 32) act_d[o] = __ldg(a.dx + o);
+        if (PRO == PRO_Q8 && a.act_smem > 0) {
+            const int qbytes = a.M * K;
+            for (int o = threadIdx.x * 16; o < qbytes; o += kGemvWarps * 32 * 16)
+                *reinterpret_cast<int4*>(act_q + o) = __ldg(reinterpret_cast<const int4*>(a.xq + o));
+            const int nd = a.M * (K / QK);
+            for (int o = threadIdx.x; o < nd; o += kGemvWarps * 32) act_d[o] = __ldg(a.dx + o);
+            __syncthreads();
+            xq = act_q;
+            dx = act_d;
+        } else if (PRO == PRO_RMS) {
+            prologue_rms<kGemvWarps>(a, act_q, act_d, part, stage);
+            xq = act_q;
+            dx = act_d;
+        } else if (PRO == PRO_SILU) {
+            prologue_silu<kGemvWarps>(a, act_q, act_d, stage);
+            xq = act_q;
+            dx = act_d;
+        }
+    }
+
+    __shared__ unsigned long long keys[EPI == EPI_ARGMAX ? kArgmaxMaxM : 1];
+    if (EPI == EPI_ARGMAX) {
+        for (int m = threadIdx.x; m < a.M; m += blockDim.x) keys[m] = 0ull;
         __syncthreads();
-        xq = act_q;
-        dx = act_d;
     }
 
     if (!SPLIT || wpp == 1) {
@@ -255,16 +504,6 @@ __global__ void __launch_bounds__(kGemvWarps * 32, kGemvCtasPerSm) q8_gemv_kerne
             const uint8_t* ra = a.rows + (r0 + 2 * p) * rs;
             const bool has_b = 2 * p + 1 < nrows;
             const uint8_t* rb = has_b ? ra + rs : ra;
-            if (a.M <= MT) {
-                float acc[2][MT];
-                acc_zero(acc);
-                for (int base = 0; base < nchunks; base += 32 * kChunks) {
-                    if (base > 0 || p != warp) pair_load(L, ra, rb, has_b, K, base, nchunks, lane);
-                    pair_compute<MT, A32>(L, a, xq, dx, base, nchunks, 0, lane, acc);
-                }
-                pair_store<MT>(a, r0 + 2 * p, has_b, 0, lane, acc);
-                continue;
-            }
             // more activation rows than one pass holds: re-read the (L2-hot)
             // row pair for each group of MT rows
             for (int m0 = 0; m0 < a.M; m0 += MT) {
@@ -275,68 +514,109 @@ __global__ void __launch_bounds__(kGemvWarps * 32, kGemvCtasPerSm) q8_gemv_kerne
                         pair_load(L, ra, rb, has_b, K, base, nchunks, lane);
                     pair_compute<MT, A32>(L, a, xq, dx, base, nchunks, m0, lane, acc);
                 }
-                pair_store<MT>(a, r0 + 2 * p, has_b, m0, lane, acc);
-            }
-        }
-        return;
-    }
-    if (!SPLIT) return;
-
-    // split-K: every warp reaches the barriers, including warps without work
-    const bool active = p < npairs && c_begin < c_end;
-    const uint8_t* ra = a.rows + (r0 + 2 * (p < npairs ? p : 0)) * rs;
-    const bool has_b = 2 * p + 1 < nrows;
-    const uint8_t* rb = has_b ? ra + rs : ra;
-    for (int m0 = 0; m0 < a.M; m0 += MT) {
-        float acc[2][MT];
-        acc_zero(acc);
-        if (active) {
-            for (int base = c_begin; base < c_end; base += 32 * kChunks) {
-                if (base > c_begin || m0 > 0) pair_load(L, ra, rb, has_b, K, base, c_end, lane);
-                pair_compute<MT, A32>(L, a, xq, dx, base, c_end, m0, lane, acc);
-            }
-        }
 #pragma unroll
-        for (int r = 0; r < 2; r++)
+                for (int r = 0; r < 2; r++)
 #pragma unroll
-            for (int j = 0; j < MT; j++) acc[r][j] = warp_sum(acc[r][j]);
-        if (lane == 0) {
+                    for (int j = 0; j < MT; j++) acc[r][j] = warp_sum(acc[r][j]);
+                if (lane == 0) {
 #pragma unroll
-            for (int r = 0; r < 2; r++)
-#pragma unroll
-                for (int j = 0; j < MT; j++) part[(warp * 2 + r) * MT + j] = acc[r][j];
-        }
-        __syncthreads();
-        if (slice == 0 && p < npairs && lane < 2 && (lane == 0 || has_b)) {
-            const int r = lane;
-            const int64_t n = r0 + 2 * p + r;
-#pragma unroll
-            for (int j = 0; j < MT; j++) {
-                const int m = m0 + j;
-                if (m < a.M) {
-                    float v = 0.0f;
-                    for (int s = 0; s < wpp; s++) v += part[((warp + s) * 2 + r) * MT + j];
-                    if (a.residual) v += a.residual[(int64_t)m * a.ldy + n];
-                    a.y[(int64_t)m * a.ldy + n] = v;
+                    for (int j = 0; j < MT; j++)
+                        if (m0 + j < a.M)
+                            epi_pair<EPI, KV>(a, m0 + j, r0 + 2 * p, has_b, acc[0][j], acc[1][j],
+                                              keys);
                 }
             }
         }
-        __syncthreads();
+    } else {
+        // split-K: every warp reaches the barriers, including warps without work
+        const bool active = p < npairs && c_begin < c_end;
+        const uint8_t* ra = a.rows + (r0 + 2 * (p < npairs ? p : 0)) * rs;
+        const bool has_b = 2 * p + 1 < nrows;
+        const uint8_t* rb = has_b ? ra + rs : ra;
+        for (int m0 = 0; m0 < a.M; m0 += MT) {
+            float acc[2][MT];
+            acc_zero(acc);
+            if (active) {
+                for (int base = c_begin; base < c_end; base += 32 * kChunks) {
+                    if (base > c_begin || m0 > 0) pair_load(L, ra, rb, has_b, K, base, c_end, lane);
+                    pair_compute<MT, A32>(L, a, xq, dx, base, c_end, m0, lane, acc);
+                }
+            }
+#pragma unroll
+            for (int r = 0; r < 2; r++)
+#pragma unroll
+                for (int j = 0; j < MT; j++) acc[r][j] = warp_sum(acc[r][j]);
+            if (lane == 0) {
+#pragma unroll
+                for (int r = 0; r < 2; r++)
+#pragma unroll
+                    for (int j = 0; j < MT; j++) part[(warp * 2 + r) * MT + j] = acc[r][j];
+            }
+            __syncthreads();
+            if (slice == 0 && p < npairs && lane == 0) {
+#pragma unroll
+                for (int j = 0; j < MT; j++) {
+                    if (m0 + j >= a.M) break;
+                    float v0 = 0.0f, v1 = 0.0f;
+                    for (int s = 0; s < wpp; s++) {
+                        v0 += part[((warp + s) * 2 + 0) * MT + j];
+                        v1 += part[((warp + s) * 2 + 1) * MT + j];
+                    }
+                    epi_pair<EPI, KV>(a, m0 + j, r0 + 2 * p, has_b, v0, v1, keys);
+                }
+            }
+            __syncthreads();
+        }
     }
+    if (EPI == EPI_ARGMAX) argmax_tail(a, keys);
 }
 
-template <int MT, bool A32>
+// Host side ---------------------------------------------------------------------
+
+inline int64_t gemv_act_bytes(int M, int64_t K) {
+    int64_t act = ((int64_t)M * K + 15) / 16 * 16 + (int64_t)M * (K / QK) * 4;
+    return (act + 127) / 128 * 128;
+}
+
+// Bytes of the fused prologue's input staging area.
+inline int64_t gemv_stage_bytes(int pro, int M, int64_t K) {
+    if (pro == PRO_RMS) return ((int64_t)M * K + K) * 4;
+    if (pro == PRO_SILU) return (int64_t)M * 2 * K * 4;
+    return 0;
+}
+
+// Whether a fused prologue (PRO_RMS / PRO_SILU) fits for M rows of K.
+inline bool gemv_fused_prologue_fits(int pro, int M, int64_t K) {
+    return M <= kGemvMaxMT && K <= kProMaxK && gemv_act_bytes(M, K) <= kGemvActSmemMax &&
+           gemv_stage_bytes(pro, M, K) <= kProStageMax;
+}
+
+template <int MT, int PRO, int EPI, typename KV>
 inline int gemv_launch_t(DeviceState* ds, GemvArgs a, cudaStream_t stream) {
     if (a.K > (1 << 24) || (int64_t)a.M * a.K > (1ll << 31))
         return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: K or M*K too large");
+    if ((PRO == PRO_RMS || PRO == PRO_SILU) && (a.M > MT || a.K > kProMaxK))
+        return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: fused prologue with M=%d, K=%lld", a.M,
+                    (long long)a.K);
+    if (EPI == EPI_ARGMAX && a.M > kArgmaxMaxM)
+        return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: argmax epilogue with M=%d > %d", a.M,
+                    kArgmaxMaxM);
     int64_t act = 0;
-    if (!A32) {
-        act = ((int64_t)a.M * a.K + 15) / 16 * 16 + (int64_t)a.M * (a.K / QK) * 4;
-        act = (act + 127) / 128 * 128;
-        if (act > kGemvActSmemMax) act = 0;
+    if (PRO != PRO_F32) {
+        act = gemv_act_bytes(a.M, a.K);
+        if (act > kGemvActSmemMax) {
+            if (PRO != PRO_Q8)
+                return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: fused prologue needs %lld B",
+                            (long long)act);
+            act = 0;
+        }
     }
     a.act_smem = (int)act;
-    const size_t smem = (size_t)kPartBytes + (size_t)act;
+    const int64_t stage = gemv_stage_bytes(PRO, a.M, a.K);
+    if (stage > kProStageMax)
+        return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: fused prologue staging needs %lld B",
+                    (long long)stage);
+    const size_t smem = (size_t)kPartBytes + (size_t)act + (size_t)stage;
     // CTAs per SM: 2 fills the SM (best for an isolated GEMV); 1 leaves room
     // for the next kernel's CTAs to co-reside and start their weight loads
     // under programmatic dependent launch.  AXQ8_GEMV_CTAS_PER_SM overrides
@@ -346,19 +626,19 @@ inline int gemv_launch_t(DeviceState* ds, GemvArgs a, cudaStream_t stream) {
         const int v = e ? atoi(e) : kGemvCtasPerSm;
         return v >= 1 && v <= 4 ? v : kGemvCtasPerSm;
     }();
+    const int64_t npt = (a.N + 1) / 2;
     int64_t grid = (int64_t)ds->sm_count * ctas_per_sm;
-    const int64_t max_grid = (a.N + 1) / 2;       // at least one row pair per CTA
-    if (grid > max_grid) grid = max_grid;
+    if (grid > npt) grid = npt;                    // at least one row pair per CTA
     // split-K inside the CTA when its row pairs cannot occupy every warp
-    const int64_t rows_per_cta = (a.N + grid - 1) / grid;
-    const bool split = 2 * ((rows_per_cta + 1) / 2) <= kGemvWarps && a.K >= 1024;
-    auto kern = split ? q8_gemv_kernel<MT, A32, true> : q8_gemv_kernel<MT, A32, false>;
+    const int64_t pairs_per_cta = (npt + grid - 1) / grid;
+    const bool split = 2 * pairs_per_cta <= kGemvWarps && a.K >= 1024;
+    auto kern = split ? q8_gemv_kernel<MT, PRO, EPI, true, KV> : q8_gemv_kernel<MT, PRO, EPI, false, KV>;
     if (smem > 48 * 1024) {
         static int configured_for[2][64] = {{0}};
         const int dev = ds->device < 64 ? ds->device : 63;
         if (!configured_for[split][dev]) {
             AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                               kPartBytes + kGemvActSmemMax),
+                                               kPartBytes + kGemvActSmemMax + kProStageMax),
                           "cudaFuncSetAttribute(q8_gemv)");
             configured_for[split][dev] = 1;
         }
@@ -368,10 +648,18 @@ inline int gemv_launch_t(DeviceState* ds, GemvArgs a, cudaStream_t stream) {
     return AXQ8_OK;
 }
 
+template <int PRO, int EPI, typename KV>
+inline int gemv_launch_mt(DeviceState* ds, const GemvArgs& a, cudaStream_t stream) {
+    if (a.M <= 1) return gemv_launch_t<1, PRO, EPI, KV>(ds, a, stream);
+    if (a.M <= 2) return gemv_launch_t<2, PRO, EPI, KV>(ds, a, stream);
+    return gemv_launch_t<4, PRO, EPI, KV>(ds, a, stream);
+}
+
+// The plain linear of the axq8 API: pre-quantized (A8) or fp32 (A32) input,
+// y = residual + x.W^T.
 inline int gemv_launch(DeviceState* ds, const GemvArgs& a, bool a32, cudaStream_t stream) {
-    if (a.M <= 1) return a32 ? gemv_launch_t<1, true>(ds, a, stream) : gemv_launch_t<1, false>(ds, a, stream);
-    if (a.M <= 2) return a32 ? gemv_launch_t<2, true>(ds, a, stream) : gemv_launch_t<2, false>(ds, a, stream);
-    return a32 ? gemv_launch_t<4, true>(ds, a, stream) : gemv_launch_t<4, false>(ds, a, stream);
+    return a32 ? gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, stream)
+               : gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, stream);
 }
 
 }  // namespace axq8

@@ -110,6 +110,11 @@ class Decoder:
     def weight_bytes_per_step(self) -> int:
         return self.lib.axdec_weight_bytes_per_step(self.h)
 
+    def step_kernels(self, n_seq: int = 1) -> int:
+        """Kernels one decode step of n_seq sequences launches (-1 before the
+        first generate/forced call with that n_seq)."""
+        return self.lib.axdec_step_kernels(self.h, n_seq)
+
     # -- decoding --------------------------------------------------------------
     def generate(self, prompts, n_new: int, logits: bool = False, stream=None):
         """Greedy continuation of prompts [n_seq, n_prompt] (or one prompt).

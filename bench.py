@@ -442,6 +442,7 @@ def run_decode_axion(args, d: Dist) -> dict:
                 "algorithmic_bytes_per_step": int(wbytes + mean_kv), "peak_source": peak_kind}
     status = ops.status()
     dev_bytes = dec.device_bytes
+    step_kernels = dec.step_kernels(1)
     dec.close()
     return {
         "metric": DECODE_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": d.world,
@@ -458,7 +459,8 @@ def run_decode_axion(args, d: Dist) -> dict:
                 "path": "axdec_generate (C ABI): host prompt in, host tokens out, "
                         "prompt positions included"},
         "roofline": roofline,
-        "gpu_launches": (1 + 10 * TL["n_layers"] + 3) * K_new,
+        "gpu_launches": step_kernels * K_new,
+        "kernels_per_step": step_kernels,
         "clocks": clk,
         "device_status": status,
         "first_tokens": [int(t) for t in toks[0][:8]],

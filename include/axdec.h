@@ -95,6 +95,11 @@ int64_t axdec_device_bytes(const axdec_model_t* m);
  * at 34 bytes per 32 weights) — the algorithmic weight traffic per token. */
 int64_t axdec_weight_bytes_per_step(const axdec_model_t* m);
 
+/* Kernels launched by one decode step of n_seq sequences: the kernel nodes
+ * of the step's CUDA graph, captured by the first axdec_generate/axdec_forced
+ * call with that n_seq (-1 before it). */
+int axdec_step_kernels(const axdec_model_t* m, int n_seq);
+
 #ifdef __cplusplus
 }
 #endif

@@ -206,6 +206,9 @@ def test_tinyllama_full_workload_runs(cuda):
     a, _, ms_a = d.generate(prompt, 256)
     b, _, ms_b = d.generate(prompt, 256)
     assert np.array_equal(a, b)
+    # embedding; per layer qkv (+RMSNorm, RoPE, KV append), attention, O,
+    # gate|up (+RMSNorm), down (+SiLU*up); LM head (+RMSNorm, argmax)
+    assert d.step_kernels(1) == 1 + 5 * 22 + 1
     assert ms_a > 0 and ms_b > 0
     assert ops.status() == 0
     d.close()
