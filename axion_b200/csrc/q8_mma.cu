@@ -1,0 +1,260 @@
+// Host side of the tensor-core Q8_0 x A8 product: TMA tensor maps, tile and
+// split-K selection, launch, and its C-ABI entry points.  Kernels in q8_mma.cuh.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <stdlib.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "q8_mma.cuh"
+#include "q8_mma.h"
+
+namespace axq8 {
+namespace {
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault,
+                                             &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            p = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    }();
+    return fn;
+}
+
+// 2-D tensor map: dim0 (innermost, contiguous) x dim1 rows, row pitch in bytes.
+int make_map(CUtensorMap* m, CUtensorMapDataType dt, const void* base, uint64_t dim0,
+             uint64_t dim1, uint64_t pitch, uint32_t box0, uint32_t box1, CUtensorMapSwizzle sw,
+             const char* what) {
+    auto fn = encode_fn();
+    if (!fn) return fail(AXQ8_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+    cuuint64_t dims[2] = {dim0, dim1};
+    cuuint64_t strides[1] = {pitch};
+    cuuint32_t box[2] = {box0, box1};
+    cuuint32_t es[2] = {1, 1};
+    CUresult r = fn(m, dt, 2, const_cast<void*>(base), dims, strides, box, es,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail(AXQ8_ERR_CUDA, "cuTensorMapEncodeTiled(%s) failed: %d", what, (int)r);
+    return AXQ8_OK;
+}
+
+int min_m() {
+    static const int v = [] {
+        const char* e = getenv("AXQ8_MMA_MIN_M");
+        const int x = e ? atoi(e) : kMmaMinM;
+        return x >= 32 ? x : kMmaMinM;
+    }();
+    return v;
+}
+
+// Per-device split-K scratch: partial tiles and tile counters (zeroed once,
+// returned to zero by every launch).
+struct SplitScratch {
+    float* part = nullptr;
+    size_t part_bytes = 0;
+    int* counters = nullptr;
+};
+constexpr int kMaxDevices = 64;
+constexpr int kCounterSlots = 1 << 16;
+SplitScratch g_split[kMaxDevices];
+std::mutex g_split_mu;
+
+int split_scratch(DeviceState* ds, size_t part_bytes, float** part, int** counters) {
+    std::lock_guard<std::mutex> lk(g_split_mu);
+    if (ds->device < 0 || ds->device >= kMaxDevices) return fail(AXQ8_ERR_INVALID, "device id");
+    SplitScratch& sc = g_split[ds->device];
+    if (!sc.counters) {
+        AXQ8_CUDA_TRY(cudaMalloc(&sc.counters, sizeof(int) * kCounterSlots), "split counters");
+        AXQ8_CUDA_TRY(cudaMemset(sc.counters, 0, sizeof(int) * kCounterSlots), "split counters");
+    }
+    if (sc.part_bytes < part_bytes) {
+        if (sc.part) {
+            AXQ8_CUDA_TRY(cudaDeviceSynchronize(), "split scratch resize");
+            cudaFree(sc.part);
+            sc.part = nullptr;
+            sc.part_bytes = 0;
+        }
+        AXQ8_CUDA_TRY(cudaMalloc(&sc.part, part_bytes), "split partials");
+        sc.part_bytes = part_bytes;
+    }
+    *part = sc.part;
+    *counters = sc.counters;
+    return AXQ8_OK;
+}
+
+template <int BN, bool DOTS>
+int launch_bn(DeviceState* ds, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& td,
+              const MmaArgs& a, dim3 grid, cudaStream_t s) {
+    auto kern = q8_mma_kernel<BN, DOTS>;
+    static int configured[kMaxDevices] = {0};
+    const int dev = ds->device < kMaxDevices ? ds->device : kMaxDevices - 1;
+    if (!configured[dev]) {
+        AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                           MmaCfg<BN>::SMEM),
+                      "cudaFuncSetAttribute(q8_mma)");
+        configured[dev] = 1;
+    }
+    AXQ8_CUDA_TRY(launch_k(kern, grid, dim3(MmaCfg<BN>::THREADS), MmaCfg<BN>::SMEM, s, true, tw,
+                           tx, td, a),
+                  "q8_mma launch");
+    return AXQ8_OK;
+}
+
+}  // namespace
+
+bool mma_eligible(const axq8_weight_t* w, int64_t M) {
+    return w && M >= min_m() && M <= (1 << 24) && w->N >= kMmaBM && w->N <= (1 << 24) &&
+           w->K >= kMmaKC && w->K % kMmaKC == 0 && w->K <= (1 << 20);
+}
+
+int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
+               int64_t M, const float* residual, float* y, int64_t ldy, int32_t* dots,
+               cudaStream_t stream) {
+    if (!w || M < 32 || w->N < kMmaBM || w->K % kMmaKC || !xq || !dxT || !y || ldy < w->N)
+        return fail(AXQ8_ERR_INVALID, "tensor-core linear: unsupported arguments");
+    if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(dxT) & 15))
+        return fail(AXQ8_ERR_INVALID, "tensor-core linear: xq/dxT not 16-byte aligned");
+    const int64_t N = w->N, K = w->K, Mp = mma_scale_pitch(M);
+    // activation rows per tile; AXQ8_MMA_BN (32/64/128) caps it for tuning
+    static const int bn_cap = [] {
+        const char* e = getenv("AXQ8_MMA_BN");
+        const int v = e ? atoi(e) : 128;
+        return v == 32 || v == 64 ? v : 128;
+    }();
+    int BN = M >= 128 ? 128 : (M >= 64 ? 64 : 32);
+    if (BN > bn_cap) BN = bn_cap;
+    CUtensorMap tw, tx, td;
+    int rc = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->rows, K, N, w->row_stride, kMmaKC,
+                      kMmaBM, CU_TENSOR_MAP_SWIZZLE_128B, "weight quants");
+    if (rc) return rc;
+    rc = make_map(&tx, CU_TENSOR_MAP_DATA_TYPE_UINT8, xq, K, M, K, kMmaKC, BN,
+                  CU_TENSOR_MAP_SWIZZLE_128B, "activation quants");
+    if (rc) return rc;
+    rc = make_map(&td, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, dxT, Mp, K / QK, Mp * 4, BN, 4,
+                  CU_TENSOR_MAP_SWIZZLE_NONE, "activation scales");
+    if (rc) return rc;
+
+    const int64_t tiles_n = (N + kMmaBM - 1) / kMmaBM, tiles_m = (M + BN - 1) / BN;
+    const int64_t tiles = tiles_n * tiles_m;
+    const int nst = (int)(K / kMmaKC);
+    const int64_t slots = (int64_t)ds->sm_count * (BN == 64 ? 2 : 1);
+    int splits = 1;
+    if (tiles < slots && !dots) {
+        splits = (int)std::min<int64_t>(slots / tiles, std::max(1, nst / 2));
+        splits = std::max(splits, 1);
+    }
+    const int per = (nst + splits - 1) / splits;
+    splits = (nst + per - 1) / per;
+    if (tiles_n > 65535) return fail(AXQ8_ERR_UNSUPPORTED, "tensor-core linear: too many tiles");
+
+    MmaArgs a = {};
+    a.rows = static_cast<const uint8_t*>(w->rows);
+    a.row_stride = w->row_stride;
+    a.N = (int)N;
+    a.K = (int)K;
+    a.M = (int)M;
+    a.stages_per_split = per;
+    a.residual = residual;
+    a.y = y;
+    a.ldy = (int)ldy;
+    a.dots = dots;
+    a.status = ds->status;
+    if (splits > 1) {
+        if (tiles > kCounterSlots)
+            return fail(AXQ8_ERR_UNSUPPORTED, "tensor-core linear: too many split tiles");
+        rc = split_scratch(ds, sizeof(float) * (size_t)splits * M * N, &a.part, &a.counters);
+        if (rc) return rc;
+    }
+    const dim3 grid((unsigned)tiles_m, (unsigned)tiles_n, (unsigned)splits);
+    if (dots) {
+        if (BN == 128) return launch_bn<128, true>(ds, tw, tx, td, a, grid, stream);
+        if (BN == 64) return launch_bn<64, true>(ds, tw, tx, td, a, grid, stream);
+        return launch_bn<32, true>(ds, tw, tx, td, a, grid, stream);
+    }
+    if (BN == 128) return launch_bn<128, false>(ds, tw, tx, td, a, grid, stream);
+    if (BN == 64) return launch_bn<64, false>(ds, tw, tx, td, a, grid, stream);
+    return launch_bn<32, false>(ds, tw, tx, td, a, grid, stream);
+}
+
+int mma_quantize(DeviceState* ds, const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,
+                 cudaStream_t stream) {
+    const int64_t nblocks = M * (K / QK);
+    int64_t grid = (nblocks + 7) / 8;
+    const int64_t cap = (int64_t)ds->sm_count * 16;
+    if (grid > cap) grid = cap;
+    AXQ8_CUDA_TRY(launch_k(quantize_act_t_kernel, dim3((unsigned)grid), dim3(256), 0, stream, true, x,
+                           (int)M, (int)K, (int)mma_scale_pitch(M), xq, dxT),
+                  "quantize_act_t launch");
+    return AXQ8_OK;
+}
+
+int mma_transpose_scales(DeviceState* ds, const float* dx, int64_t M, int64_t K, float* dxT,
+                         cudaStream_t stream) {
+    const int64_t total = M * (K / QK);
+    int64_t grid = (total + 255) / 256;
+    const int64_t cap = (int64_t)ds->sm_count * 8;
+    if (grid > cap) grid = cap;
+    AXQ8_CUDA_TRY(launch_k(transpose_scales_kernel, dim3((unsigned)grid), dim3(256), 0, stream, true,
+                           dx, (int)M, (int)(K / QK), (int)mma_scale_pitch(M), dxT),
+                  "transpose_scales launch");
+    return AXQ8_OK;
+}
+
+}  // namespace axq8
+
+// ---- C ABI ------------------------------------------------------------------------
+
+using namespace axq8;
+
+extern "C" {
+
+int axq8_linear_path(const axq8_weight_t* w, int64_t M, int act_mode) {
+    if (!w || M < 0) return fail(AXQ8_ERR_INVALID, "axq8_linear_path: bad argument");
+    return act_mode == AXQ8_ACT_Q8 && mma_eligible(w, M) ? AXQ8_PATH_TENSOR_CORE : AXQ8_PATH_GEMV;
+}
+
+int axq8_quantize_act_t(const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,
+                        void* stream) {
+    if (M <= 0 || K <= 0 || K % QK || M > (1 << 24) || K > (1 << 20))
+        return fail(AXQ8_ERR_INVALID, "axq8_quantize_act_t: bad shape [%lld, %lld]", (long long)M,
+                    (long long)K);
+    if (!x || !xq || !dxT) return fail(AXQ8_ERR_INVALID, "axq8_quantize_act_t: null pointer");
+    DeviceState* ds = device_state();
+    if (!ds) return AXQ8_ERR_CUDA;
+    return mma_quantize(ds, x, M, K, xq, dxT, static_cast<cudaStream_t>(stream));
+}
+
+int axq8_linear_q8act_t(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
+                        const float* residual, float* y, void* stream) {
+    if (!w || !w->rows) return fail(AXQ8_ERR_INVALID, "axq8_linear_q8act_t: null weight");
+    if (w->row_stride != q8r_row_stride(w->K) || (reinterpret_cast<uintptr_t>(w->rows) & 15))
+        return fail(AXQ8_ERR_INVALID, "axq8_linear_q8act_t: weight not in the repacked layout");
+    if (M < 32 || w->N < kMmaBM || w->K % kMmaKC)
+        return fail(AXQ8_ERR_UNSUPPORTED,
+                    "axq8_linear_q8act_t: needs M >= 32, N >= 128, K %% 128 == 0 (M=%lld N=%lld K=%lld)",
+                    (long long)M, (long long)w->N, (long long)w->K);
+    DeviceState* ds = device_state();
+    if (!ds) return AXQ8_ERR_CUDA;
+    return mma_linear(ds, w, xq, dxT, M, residual, y, w->N, nullptr,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int axq8_block_dots_tc(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
+                       int32_t* dots, float* y, void* stream) {
+    if (!w || !w->rows || !dots || !y) return fail(AXQ8_ERR_INVALID, "axq8_block_dots_tc: null argument");
+    if (w->row_stride != q8r_row_stride(w->K) || (reinterpret_cast<uintptr_t>(w->rows) & 15))
+        return fail(AXQ8_ERR_INVALID, "axq8_block_dots_tc: weight not in the repacked layout");
+    if (M < 32 || w->N < kMmaBM || w->K % kMmaKC)
+        return fail(AXQ8_ERR_UNSUPPORTED, "axq8_block_dots_tc: needs M >= 32, N >= 128, K %% 128 == 0");
+    DeviceState* ds = device_state();
+    if (!ds) return AXQ8_ERR_CUDA;
+    return mma_linear(ds, w, xq, dxT, M, nullptr, y, w->N, dots, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

@@ -1,0 +1,40 @@
+// Host interface of the tensor-core (tcgen05 kind::i8) Q8_0 x A8 product,
+// used by the C ABI in q8_linear.cu and by the decoder.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "axq8.h"
+#include "runtime.h"
+
+namespace axq8 {
+
+// Smallest M routed to the tensor-core path by default (AXQ8_MMA_MIN_M
+// overrides it; a large value keeps every M on the GEMV).
+constexpr int kMmaMinM = 32;
+
+// Whether the tensor-core path handles w at M rows: M >= the threshold,
+// N >= 128, K a multiple of 128.
+bool mma_eligible(const axq8_weight_t* w, int64_t M);
+
+// y[M][ldy] = residual + xq . W^T with xq [M][K] int8 (16-byte aligned rows)
+// and the activation scales transposed, dxT [K/32][Mp] fp32 (Mp = M rounded
+// up to 4).  dots, when not null, receives every raw int32 block dot
+// [M][N][K/32].  Requires the shape part of mma_eligible (any M >= 32).
+int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
+               int64_t M, const float* residual, float* y, int64_t ldy, int32_t* dots,
+               cudaStream_t stream);
+
+// Mp for a given M (row pitch of dxT).
+inline int64_t mma_scale_pitch(int64_t M) { return (M + 3) / 4 * 4; }
+
+// Quantize x [M][K] into xq [M][K] and dxT [K/32][Mp] (A8 convention).
+int mma_quantize(DeviceState* ds, const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,
+                 cudaStream_t stream);
+
+// dx [M][K/32] -> dxT [K/32][Mp].
+int mma_transpose_scales(DeviceState* ds, const float* dx, int64_t M, int64_t K, float* dxT,
+                         cudaStream_t stream);
+
+}  // namespace axq8

@@ -226,6 +226,71 @@ def block_dots(weight: Q8Weight, xq: torch.Tensor) -> torch.Tensor:
     return out
 
 
+PATHS = {_lib.AXQ8_PATH_GEMV: "gemv", _lib.AXQ8_PATH_TENSOR_CORE: "tensor_core"}
+
+
+def linear_path(weight: Q8Weight, M: int, act_mode: str = "q8") -> str:
+    """Which kernel linear_from_gguf runs at M rows: "gemv" or "tensor_core"."""
+    rc = _lib.load().axq8_linear_path(weight.c, M, ACT_MODES[act_mode])
+    if rc < 0:
+        check(rc)
+    return PATHS[rc]
+
+
+def scale_pitch(M: int) -> int:
+    """Row pitch of the transposed activation scales (M rounded up to 4)."""
+    return (M + 3) // 4 * 4
+
+
+def quantize_activations_t(x: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """A8 quantization for the tensor-core product: (xq int8 [M,K],
+    dxT fp32 [K/32, Mp]) with the scales transposed."""
+    _require_cuda(x, "quantize_activations_t input")
+    if x.dim() != 2 or x.shape[1] % QK or x.dtype != torch.float32:
+        raise RuntimeError("quantize_activations_t expects float32 [M, K] with K % 32 == 0")
+    x = x.contiguous()
+    M, K = x.shape
+    xq = torch.empty(M, K, dtype=torch.int8, device=x.device)
+    dxT = torch.empty(K // QK, scale_pitch(M), dtype=torch.float32, device=x.device)
+    with torch.cuda.device(x.device):
+        check(_lib.load().axq8_quantize_act_t(C.c_void_p(x.data_ptr()), M, K,
+                                              C.c_void_p(xq.data_ptr()),
+                                              C.c_void_p(dxT.data_ptr()), C.c_void_p(_stream())))
+    return xq, dxT
+
+
+def linear_q8act_t(weight: Q8Weight, xq: torch.Tensor, dxT: torch.Tensor,
+                   residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Tensor-core product y = residual + dequant(xq, dxT) . W^T (M >= 32)."""
+    _require_cuda(xq, "xq")
+    M = xq.shape[0]
+    if xq.shape[1] != weight.K:
+        raise RuntimeError("linear_from_gguf dimension mismatch: input K != weight K")
+    out = torch.empty(M, weight.N, dtype=torch.float32, device=xq.device)
+    res = residual.contiguous() if residual is not None else None
+    with torch.cuda.device(xq.device):
+        check(_lib.load().axq8_linear_q8act_t(weight.c, C.c_void_p(xq.data_ptr()),
+                                              C.c_void_p(dxT.data_ptr()), M,
+                                              C.c_void_p(_ptr(res)) if res is not None else None,
+                                              C.c_void_p(out.data_ptr()), C.c_void_p(_stream())))
+    return out
+
+
+def block_dots_tc(weight: Q8Weight, xq: torch.Tensor,
+                  dxT: torch.Tensor) -> tuple[torch.Tensor, torch.Tensor]:
+    """Block dots read back from the tensor cores: (dots int32 [M, N, K/32], y)."""
+    _require_cuda(xq, "xq")
+    M = xq.shape[0]
+    dots = torch.empty(M, weight.N, weight.K // QK, dtype=torch.int32, device=xq.device)
+    y = torch.empty(M, weight.N, dtype=torch.float32, device=xq.device)
+    with torch.cuda.device(xq.device):
+        check(_lib.load().axq8_block_dots_tc(weight.c, C.c_void_p(xq.contiguous().data_ptr()),
+                                             C.c_void_p(dxT.data_ptr()), M,
+                                             C.c_void_p(dots.data_ptr()), C.c_void_p(y.data_ptr()),
+                                             C.c_void_p(_stream())))
+    return dots, y
+
+
 class QuantType(enum.Enum):
     """Runtime per-tensor formats (quantized_matmul.hpp:14-19); Q8_0 runs on device."""
     FP32 = 0

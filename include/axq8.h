@@ -91,9 +91,33 @@ int axq8_quantize_act(const float* x, int64_t M, int64_t K, int8_t* xq, float* d
  * the quantized activations live in a per-device workspace that this
  * library allocates on first use and grows when a larger M*K arrives (the
  * only allocation on this path); calls on different streams of one device
- * must not overlap.  Decode (M <= 64) runs the streaming GEMV kernel. */
+ * must not overlap.  A8 with M >= 32, N >= 128 and K % 128 == 0 runs the
+ * tensor-core product (tcgen05 kind::i8, axq8_linear_q8act_t); everything
+ * else runs the streaming GEMV kernel (axq8_linear_path tells which). */
 int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int act_mode,
                 void* stream);
+
+/* Which kernel axq8_linear runs for w at M rows in act_mode. */
+enum {
+    AXQ8_PATH_GEMV = 0,
+    AXQ8_PATH_TENSOR_CORE = 1
+};
+int axq8_linear_path(const axq8_weight_t* w, int64_t M, int act_mode);
+
+/* A8 quantization for the tensor-core product: xq[M, K] int8 as
+ * axq8_quantize_act, the scales transposed: dxT[K/32, Mp] fp32 with
+ * Mp = M rounded up to a multiple of 4. */
+int axq8_quantize_act_t(const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,
+                        void* stream);
+
+/* y[M, N] = residual + xq.W^T on the tensor cores (prefill / batched decode:
+ * linear_from_gguf, linear.cpp:27-71, at M >= 32), from axq8_quantize_act_t
+ * output.  Needs M >= 32, N >= 128, K % 128 == 0 (else AXQ8_ERR_UNSUPPORTED).
+ * Exact int32 block dots; fp32 combination acc += (D_b*dw)*dx per block.
+ * Few output tiles split K across CTAs through a per-device scratch this
+ * library allocates on first use. */
+int axq8_linear_q8act_t(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
+                        const float* residual, float* y, void* stream);
 
 /* Same with pre-quantized activations (xq[M,K] int8, dx[M,K/32] fp32), as
  * written by axq8_quantize_act or a fused producer.  `residual` (nullable,
@@ -119,6 +143,12 @@ int axq8_linear_noalloc(const axq8_weight_t* w, const float* x, int64_t M, float
  * 32-block; a debug/parity entry point (slow). */
 int axq8_block_dots(const axq8_weight_t* w, const int8_t* xq, int64_t M, int32_t* dots,
                     void* stream);
+
+/* The same block dots read back from the tensor cores' TMEM accumulators
+ * (axq8_linear_q8act_t's kernel in a debug mode that also stores every
+ * int32 block result; y receives the product).  Same shape limits. */
+int axq8_block_dots_tc(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
+                       int32_t* dots, float* y, void* stream);
 
 /* Per-tensor Q8_0 runtime format of quantize_weight / quantized_matmul
  * (quantized_matmul.cpp:35-204, QuantType::Q8_0): W[K, N] fp32 ->

@@ -75,3 +75,28 @@ def test_invalid_arguments_fail_cleanly():
     assert b"K" in lib.axq8_last_error() or b"null" in lib.axq8_last_error()
     rc = lib.axq8_linear(None, None, 1, None, 0, None)
     assert rc == _lib.AXQ8_ERR_INVALID
+
+
+def test_tensor_core_entry_points_validate_shapes():
+    """The tensor-core product refuses shapes it does not tile (M < 32,
+    N < 128, K % 128 != 0) before touching the device; axq8_linear_path is
+    pure host logic."""
+    from axion_b200 import _lib
+    lib = _lib.load()
+    w = _lib.axq8_weight_t()
+    w.rows = 4096                      # never dereferenced on these paths
+    w.N, w.K, w.row_stride = 256, 256, lib.axq8_row_stride(256)
+    w.owns, w.device = 0, 0
+    rc = lib.axq8_linear_q8act_t(ctypes.byref(w), 4096, 4096, 16, None, 4096, None)
+    assert rc == _lib.AXQ8_ERR_UNSUPPORTED and b"M >= 32" in lib.axq8_last_error()
+    w.N = 64
+    rc = lib.axq8_linear_q8act_t(ctypes.byref(w), 4096, 4096, 64, None, 4096, None)
+    assert rc == _lib.AXQ8_ERR_UNSUPPORTED
+    w.N, w.K, w.row_stride = 256, 96, lib.axq8_row_stride(96)
+    rc = lib.axq8_block_dots_tc(ctypes.byref(w), 4096, 4096, 64, 4096, 4096, None)
+    assert rc == _lib.AXQ8_ERR_UNSUPPORTED
+    w.K, w.row_stride = 256, lib.axq8_row_stride(256)
+    assert lib.axq8_linear_path(ctypes.byref(w), 1, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_GEMV
+    assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_TENSOR_CORE
+    assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_F32) == _lib.AXQ8_PATH_GEMV
+    assert lib.axq8_quantize_act_t(None, 4, 33, None, None, None) == _lib.AXQ8_ERR_INVALID
