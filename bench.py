@@ -2,7 +2,7 @@
 """Benchmark of the B200 Q8_0 hot path; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl axion|reference]
-                    [--workload decode|gemv]
+                    [--workload decode|gemv|prefill]
 
 Workloads
   decode (default) TinyLlama-1.1B-architecture decode: 22
@@ -23,6 +23,13 @@ Workloads
          weight rotates over enough copies (> 4 x L2) that every step streams
          its weight from HBM.  Metric: algorithmic bytes / s (W 34/32 B per
          weight + x + y = 12,285,952 B per step).
+  prefill Q8_0 prefill GEMM sweep: Llama-2-7B linear
+         shapes [4096x4096], [11008x4096], [4096x11008], [32000x4096] x M in
+         {256, 1024, 2048, 4096} on the tcgen05 kind::i8 path.  One step = one
+         GEMM (cases in rotation; default K = 16 = the whole sweep).  Metric:
+         int8 TOPS (2*M*N*K / device time); roofline against the int8 dense
+         peak; the reference arm times linear_from_gguf on [4096x4096] for a
+         bounded M.
 
 Arms
   --impl axion      the CUDA path (libaxq8.so) on N GPUs, one process per GPU
@@ -529,12 +536,182 @@ def decode_reference(args, steps: int) -> dict:
             "seconds": round(sec, 3), "steps": positions}
 
 
+# ---------------------------------------------------------------------------
+# Prefill GEMM sweep: Llama-2-7B linear shapes on the
+# tensor-core path
+# ---------------------------------------------------------------------------
+
+PREFILL_SHAPES = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+PREFILL_MS = [256, 1024, 2048, 4096]
+PREFILL_METRIC = "Q8_0 prefill GEMM int8 TOPS (Llama-2-7B linear shapes x M sweep)"
+PREFILL_CONFIG = {"workload": "q8_0_prefill_gemm_sweep_llama2_7b",
+                  "shapes_NxK": [f"{n}x{k}" for n, k in PREFILL_SHAPES], "M": PREFILL_MS}
+
+
+def run_prefill_axion(args, d: Dist) -> dict:
+    """One step = one GEMM of the sweep (cases in rotation: 4 shapes x 4 M,
+    253 MB of Q8_0 weights plus up to 180 MB of activations, so consecutive
+    GEMMs never find their operands in L2).  value: sum of 2*M*N*K over the
+    timed GEMMs / their summed device time through axq8_linear (activation
+    quantization included).  roofline: the tcgen05 kernel alone
+    (axq8_linear_q8act_t on pre-quantized activations) against the int8 dense
+    peak taken as 2 x the measured bf16 GEMM peak (B200 int8:bf16 dense rate
+    2:1)."""
+    import torch
+    from axion_b200 import _lib, ops
+    lib = _lib.load()
+    dev = torch.device("cuda", d.local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    s_ptr = C.c_void_p(stream.cuda_stream)
+    cases = [(n, k, m) for (n, k) in PREFILL_SHAPES for m in PREFILL_MS]
+    with torch.cuda.stream(stream):
+        weights = {(n, k): ops.Q8Weight.synthetic(0xA710 + i, n, k, device=dev)
+                   for i, (n, k) in enumerate(PREFILL_SHAPES)}
+        g = torch.Generator(device=dev).manual_seed(7 + d.rank)
+        xs = {k: torch.randn(max(PREFILL_MS), k, generator=g, device=dev)
+              for k in {k for _, k in PREFILL_SHAPES}}
+        ys = torch.empty(max(PREFILL_MS) * max(n for n, _ in PREFILL_SHAPES), device=dev)
+    K_steps, W_steps = args.steps, args.warmup
+
+    def gemm(i):
+        n, k, m = cases[i % len(cases)]
+        _lib.check(lib.axq8_linear(weights[(n, k)].c, C.c_void_p(xs[k].data_ptr()), m,
+                                   C.c_void_p(ys.data_ptr()), _lib.AXQ8_ACT_Q8, s_ptr))
+        return 2.0 * m * n * k
+
+    # untimed set-up pass over every case: the library's workspaces reach their
+    # final size here, not inside the timed region
+    for i in range(len(cases)):
+        gemm(i)
+    for i in range(W_steps):
+        gemm(i)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device_uuid(dev)).start()
+    time.sleep(0.15)
+    d.barrier()
+    torch.cuda.synchronize()
+    evs = [torch.cuda.Event(enable_timing=True) for _ in range(K_steps + 1)]
+    ops_total = 0.0
+    evs[0].record(stream)
+    for i in range(K_steps):
+        ops_total += gemm(W_steps + i)
+        evs[i + 1].record(stream)
+    torch.cuda.synchronize()
+    d.barrier()
+    clk = clocks.stop()
+    per = [evs[i].elapsed_time(evs[i + 1]) for i in range(K_steps)]
+    ms = d.max(sum(per))
+    value = (d.sum(ops_total) if d.world > 1 else ops_total) / (ms / 1e3) / 1e12
+    sweep = []
+    for i in range(K_steps):
+        n, k, m = cases[(W_steps + i) % len(cases)]
+        sweep.append({"N": n, "K": k, "M": m, "us": round(per[i] * 1e3, 1),
+                      "tops": round(2.0 * m * n * k / (per[i] / 1e3) / 1e12, 1)})
+
+    # --- roofline: the tensor-core kernel alone on pre-quantized activations
+    with torch.cuda.stream(stream):
+        qa = {}
+        for (n, k, m) in cases:
+            if (k, m) not in qa:
+                qa[(k, m)] = ops.quantize_activations_t(xs[k][:m])
+    torch.cuda.synchronize()
+    k_ops, k_ms = 0.0, 0.0
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    for (n, k, m) in cases:
+        xq, dxT = qa[(k, m)]
+        e0.record(stream)
+        _lib.check(lib.axq8_linear_q8act_t(weights[(n, k)].c, C.c_void_p(xq.data_ptr()),
+                                           C.c_void_p(dxT.data_ptr()), m, None,
+                                           C.c_void_p(ys.data_ptr()), s_ptr))
+        e1.record(stream)
+        torch.cuda.synchronize()
+        k_ms += e0.elapsed_time(e1)
+        k_ops += 2.0 * m * n * k
+    peaks, peak_kind = measured_peaks()
+    int8_peak = 2.0 * peaks["bf16_tflops"]
+    achieved = k_ops / (k_ms / 1e3) / 1e12
+    roofline = {"bound": "tensor", "achieved": round(achieved, 1), "peak": round(int8_peak, 1),
+                "unit": "TOPS", "frac": round(achieved / int8_peak, 4),
+                "traffic": ncu_traffic(PREFILL_CONFIG["workload"]),
+                "kernel": "q8_mma_kernel (tcgen05.mma kind::i8)",
+                "peak_source": f"2 x {peak_kind} bf16 GEMM peak (int8 dense rate = 2 x bf16)",
+                "kernel_ms_sweep": round(k_ms, 3)}
+
+    # --- e2e: the same GEMMs through axq8_linear from pinned host memory
+    xh = {k: torch.empty(max(PREFILL_MS), k, pin_memory=True) for k in xs}
+    for k in xs:
+        xh[k].copy_(xs[k].cpu())
+    yh = torch.empty(ys.numel(), pin_memory=True)
+    xd = {k: torch.empty_like(xs[k]) for k in xs}
+    h2d = d2h = 0
+    e2e_ops = 0.0
+    with torch.cuda.stream(stream):
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for i in range(K_steps):
+            n, k, m = cases[(W_steps + i) % len(cases)]
+            xd[k][:m].copy_(xh[k][:m], non_blocking=True)
+            _lib.check(lib.axq8_linear(weights[(n, k)].c, C.c_void_p(xd[k].data_ptr()), m,
+                                       C.c_void_p(ys.data_ptr()), _lib.AXQ8_ACT_Q8, s_ptr))
+            yh[:m * n].copy_(ys[:m * n], non_blocking=True)
+            h2d += m * k * 4
+            d2h += m * n * 4
+            e2e_ops += 2.0 * m * n * k
+        e1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = d.max(e0.elapsed_time(e1))
+    e2e_val = (d.sum(e2e_ops) if d.world > 1 else e2e_ops) / (e2e_ms / 1e3) / 1e12
+    return {
+        "metric": PREFILL_METRIC, "value": round(value, 1), "unit": "TOPS", "n_gpus": d.world,
+        "steps": K_steps, "warmup": W_steps, "ms_per_step": round(ms / K_steps, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32 (tcgen05 kind::i8) -> fp32 per-block rescale",
+        "data": "synthetic (device-generated Q8_0 weights N(0,0.02); activations N(0,1))",
+        "config": dict(PREFILL_CONFIG, parallelism=f"replicas x{d.world}",
+                       l2_policy="cases in rotation, 253 MB of weights > L2"),
+        "e2e": {"value": round(e2e_val, 1), "unit": "TOPS", "h2d_bytes_per_step": h2d // K_steps,
+                "d2h_bytes_per_step": d2h // K_steps,
+                "path": "axq8_linear (C ABI), pinned H2D of x and D2H of y per GEMM"},
+        "roofline": roofline,
+        "gpu_launches": 2 * K_steps,
+        "clocks": clk,
+        "device_status": ops.status(),
+        "sweep": sweep,
+    }
+
+
+def prefill_reference(args, steps: int) -> dict:
+    """linear_from_gguf of the reference (load_tensor + fp32 GEMM) on the
+    [4096 x 4096] shape with a bounded M (`steps` rows), host cores."""
+    import numpy as np
+    from axion_b200.gguf import Q8_0, GGUFWriter
+    from oracle.oracle import Oracle, RefLib
+    o, r = Oracle(), RefLib()
+    tmp = Path(tempfile.mkdtemp()) / "prefill.gguf"
+    gw = GGUFWriter()
+    gw.add_tensor("blk.0.attn_q.weight", o.synth_q8_0(0xA710, 4096, 4096), (4096, 4096), Q8_0)
+    gw.write(tmp)
+    x = np.random.default_rng(0).normal(0, 1, (steps, 4096)).astype(np.float32)
+    r.time_linear(tmp, "blk.0.attn_q.weight", x[:1], 4096, 1)
+    sec, _ = r.time_linear(tmp, "blk.0.attn_q.weight", x, 4096, 1)
+    tmp.unlink()
+    ops_ = 2.0 * steps * 4096 * 4096
+    return {"value": round(ops_ / sec / 1e12, 6), "unit": "TOPS", "cores": host_cores(),
+            "kind": "reference",
+            "sample": f"GGUFLoader::load_tensor + linear_from_gguf, [4096x4096] Q8_0, M={steps}, "
+                      f"OpenMP threads={host_cores()}",
+            "seconds": round(sec, 3), "steps": 1}
+
+
 WORKLOADS = {
     # name: (axion arm, reference/cpu-baseline arm, metric, config, default K, reference sample)
     "decode": (run_decode_axion, decode_reference, DECODE_METRIC, DECODE_CONFIG, TL_NEW, 3),
     "gemv": (run_gemv_axion, gemv_reference, "Q8_0 GEMV HBM GB/s (algorithmic bytes)",
              {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K, "M": 1},
              200000, 300),
+    "prefill": (run_prefill_axion, prefill_reference, PREFILL_METRIC, PREFILL_CONFIG, 16, 64),
 }
 
 

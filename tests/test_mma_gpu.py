@@ -67,7 +67,7 @@ def test_quantize_act_t_bit_exact(cuda, oracle):
         assert np.array_equal(dxT.cpu().numpy()[:, :M].view(np.uint32), od.T.view(np.uint32))
 
 
-@pytest.mark.parametrize("N,K,M", [(128, 128, 32), (200, 1024, 100), (384, 512, 129)])
+@pytest.mark.parametrize("N,K,M", [(128, 128, 32), (200, 1024, 100), (384, 512, 129), (256, 256, 520)])
 def test_tensor_core_block_dots_bit_exact(cuda, oracle, N, K, M):
     ops = _ops()
     blocks, x, w = _case(oracle, N, K, M, seed=N + M)
