@@ -43,6 +43,7 @@ class axdec_config_t(C.Structure):
         ("vocab", C.c_int32), ("rope_theta", C.c_float), ("rms_eps", C.c_float),
         ("max_batch", C.c_int32), ("max_ctx", C.c_int32), ("kv_block", C.c_int32),
         ("act_mode", C.c_int32), ("kv_fp32", C.c_int32),
+        ("tp_size", C.c_int32), ("tp_rank", C.c_int32),
     ]
 
 
@@ -82,6 +83,8 @@ SIGNATURES: dict[str, tuple] = {
     "axdec_device_bytes": (_I64, [_P]),
     "axdec_weight_bytes_per_step": (_I64, [_P]),
     "axdec_step_kernels": (_I32, [_P, _I32]),
+    "axdec_tp_unique_id": (_I32, [_P, _I64]),
+    "axdec_tp_connect": (_I32, [_P, _P]),
     "axq8_status_read": (_I32, [C.POINTER(C.c_int)]),
     "axq8_status_clear": (_I32, []),
     "axq8_last_error": (C.c_char_p, []),

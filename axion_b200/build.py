@@ -40,12 +40,13 @@ def nvcc() -> str:
 
 
 def nccl_include() -> list[str]:
-    """NCCL header location (torch's bundled NCCL, else the system one)."""
+    """NCCL header location and the directory of its library (torch's bundled
+    NCCL, else the system one); the library is opened at run time."""
     try:
         import nvidia.nccl  # type: ignore
-        inc = Path(list(nvidia.nccl.__path__)[0]) / "include"
-        if (inc / "nccl.h").exists():
-            return [f"-I{inc}"]
+        root = Path(list(nvidia.nccl.__path__)[0])
+        if (root / "include" / "nccl.h").exists():
+            return [f"-I{root / 'include'}", f'-DAXQ8_NCCL_DIR="{root / "lib"}"']
     except Exception:
         pass
     return []
@@ -82,7 +83,7 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
         objs = list(ex.map(lambda s: _compile(s, force, hm), srcs))
     newest = max(o.stat().st_mtime for o in objs)
     if force or not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs)]
+        cmd = [nvcc(), *ARCH, "-shared", "-cudart", "static", "-o", str(LIB), *map(str, objs), "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")

@@ -276,6 +276,33 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
     if ((lane % (32 / DL)) == 0) dx[base / QK] = __fdiv_rn(am, 127.0f);
 }
 
+// ---- greedy step advance after a cross-rank argmax ------------------------------
+// The tensor-parallel LM head leaves each sequence's packed (logit, global
+// index) key in amax_key; after the max all-reduce over ranks one thread
+// performs the advance of the single-GPU argmax epilogue: record the token,
+// feed the next input (prompt token or the argmax), move the position, and
+// zero the key for the next step.
+__global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key, int M,
+                                      int* __restrict__ pos, int* __restrict__ tokens,
+                                      const int* __restrict__ feed, const int* __restrict__ ctl,
+                                      int* __restrict__ out_tokens, int* __restrict__ argmax_out) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int n_prompt = ctl[0], feed_len = ctl[1], max_out = ctl[2];
+    for (int m = 0; m < M; m++) {
+        const unsigned long long k = amax_key[m];
+        amax_key[m] = 0ull;
+        const int idx = k == 0ull ? 0 : argmax_key_index(k);
+        const int p = pos[m];
+        const int np = p + 1;
+        argmax_out[m] = idx;
+        if (np >= n_prompt && np - n_prompt < max_out) out_tokens[m * max_out + (np - n_prompt)] = idx;
+        tokens[m] = np < feed_len ? feed[m * feed_len + np] : idx;
+        pos[m] = np;
+    }
+}
+
 // ---- SiLU(gate) * up (+ A8 quantization) -------------------------------------------
 // gu row = [gate (F) | up (F)].  a = (g / (1 + e^-g)) * u, rounded per op as
 // silu.cpp and elementwise.cpp do.  One warp per 32-block.

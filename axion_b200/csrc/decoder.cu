@@ -34,6 +34,7 @@
 #include "axq8.h"
 #include "common.cuh"
 #include "decode_ops.cuh"
+#include "nccl_dl.h"
 #include "q8_gemv.cuh"
 #include "runtime.h"
 
@@ -62,7 +63,10 @@ struct Graph {
 }  // namespace
 
 struct axdec_model {
-    axdec_config_t c{};
+    axdec_config_t c{};           // this rank's dimensions (heads, ffn, vocab divided by tp)
+    axdec_config_t cf{};          // the whole model's dimensions
+    int tp = 1, rank = 0;
+    ncclComm_t comm = nullptr;    // tensor-parallel communicator (tp > 1)
     DeviceState* ds = nullptr;
     int Nq = 0, Nkv = 0, Nqkv = 0;
     int64_t rs_h = 0, rs_q = 0, rs_f = 0;
@@ -142,14 +146,38 @@ struct Dest {
     float* f32 = nullptr;   // norm weight destination
     int64_t n = 0;
     bool rope_perm = false; // attn_q / attn_k: rows permuted for the RoPE epilogue
+    // this rank's slice of the whole [src_N, src_K] tensor (rows src_row0..,
+    // columns src_col0..); the whole tensor when not split
+    int64_t src_row0 = 0, src_col0 = 0, src_N = 0, src_K = 0;
 };
 
 int resolve(axdec_model* m, const char* name, Dest* d) {
     const axdec_config_t& c = m->c;
-    const int H = c.hidden, F = c.ffn;
-    if (!strcmp(name, "token_embd.weight")) { *d = {m->embd, 0, c.vocab, H}; return 0; }
-    if (!strcmp(name, "output.weight")) { *d = {m->out_w, 0, c.vocab, H}; return 0; }
-    if (!strcmp(name, "output_norm.weight")) { d->f32 = m->out_norm; d->n = H; return 0; }
+    const int H = c.hidden, F = c.ffn, r = m->rank;
+    const int64_t Vf = m->cf.vocab, Nqf = (int64_t)m->cf.n_heads * c.head_dim,
+                  Nkvf = (int64_t)m->cf.n_kv_heads * c.head_dim, Ff = m->cf.ffn;
+    auto rows_slice = [&](uint8_t* rows, int64_t row0, int64_t n, int64_t src_n, int64_t src_row0) {
+        *d = Dest{};
+        d->rows = rows;
+        d->row0 = row0;
+        d->N = n;
+        d->K = H;
+        d->src_row0 = src_row0;
+        d->src_N = src_n;
+        d->src_K = H;
+    };
+    auto cols_slice = [&](uint8_t* rows, int64_t k, int64_t src_k, int64_t src_col0) {
+        *d = Dest{};
+        d->rows = rows;
+        d->N = H;
+        d->K = k;
+        d->src_col0 = src_col0;
+        d->src_N = H;
+        d->src_K = src_k;
+    };
+    if (!strcmp(name, "token_embd.weight")) { rows_slice(m->embd, 0, Vf, Vf, 0); return 0; }
+    if (!strcmp(name, "output.weight")) { rows_slice(m->out_w, 0, c.vocab, Vf, (int64_t)r * c.vocab); return 0; }
+    if (!strcmp(name, "output_norm.weight")) { *d = Dest{}; d->f32 = m->out_norm; d->n = H; return 0; }
     int layer;
     std::string slot;
     if (!parse_layer_name(name, &layer, &slot) || layer < 0 || layer >= c.n_layers)
@@ -157,17 +185,32 @@ int resolve(axdec_model* m, const char* name, Dest* d) {
     Layer& Ly = m->L[layer];
     const int si = slot_index(slot);
     switch (si) {
-        case 0: d->f32 = Ly.attn_norm; d->n = H; return 0;
-        case 5: d->f32 = Ly.ffn_norm; d->n = H; return 0;
-        case 1: *d = {Ly.qkv, 0, m->Nq, H}; d->rope_perm = true; return 0;
-        case 2: *d = {Ly.qkv, m->Nq, m->Nkv, H}; d->rope_perm = true; return 0;
-        case 3: *d = {Ly.qkv, m->Nq + m->Nkv, m->Nkv, H}; return 0;
-        case 4: *d = {Ly.o, 0, H, m->Nq}; return 0;
-        case 6: *d = {Ly.gu, 0, F, H}; return 0;
-        case 7: *d = {Ly.gu, F, F, H}; return 0;
-        case 8: *d = {Ly.down, 0, H, F}; return 0;
+        case 0: *d = Dest{}; d->f32 = Ly.attn_norm; d->n = H; return 0;
+        case 5: *d = Dest{}; d->f32 = Ly.ffn_norm; d->n = H; return 0;
+        case 1: rows_slice(Ly.qkv, 0, m->Nq, Nqf, (int64_t)r * m->Nq); d->rope_perm = true; return 0;
+        case 2: rows_slice(Ly.qkv, m->Nq, m->Nkv, Nkvf, (int64_t)r * m->Nkv); d->rope_perm = true; return 0;
+        case 3: rows_slice(Ly.qkv, m->Nq + m->Nkv, m->Nkv, Nkvf, (int64_t)r * m->Nkv); return 0;
+        case 4: cols_slice(Ly.o, m->Nq, Nqf, (int64_t)r * m->Nq); return 0;
+        case 6: rows_slice(Ly.gu, 0, F, Ff, (int64_t)r * F); return 0;
+        case 7: rows_slice(Ly.gu, F, F, Ff, (int64_t)r * F); return 0;
+        case 8: cols_slice(Ly.down, F, Ff, (int64_t)r * F); return 0;
         default: return fail(AXQ8_ERR_INVALID, "axdec: unknown tensor '%s'", name);
     }
+}
+
+int nccl_check(ncclResult_t r, const char* what) {
+    if (r == ncclSuccess) return AXQ8_OK;
+    const NcclApi* api = nccl_api();
+    return fail(AXQ8_ERR_CUDA, "%s: %s", what, api ? api->GetErrorString(r) : "NCCL error");
+}
+
+// Sum this rank's partial [M, H] hidden state over the tensor-parallel ranks, in place.
+int allreduce_hidden(axdec_model* m, int M, cudaStream_t s) {
+    const NcclApi* api = nccl_api();
+    if (!api) return AXQ8_ERR_UNSUPPORTED;
+    return nccl_check(api->AllReduce(m->h, m->h, (size_t)M * m->c.hidden, ncclFloat, ncclSum,
+                                     m->comm, s),
+                      "axdec: hidden all-reduce");
 }
 
 __global__ void fill_kernel(float* p, int64_t n, float v) {
@@ -279,8 +322,11 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
     DeviceState* ds = m->ds;
     int rc;
     AXQ8_CUDA_TRY(launch_k(embed_kernel, dim3(M), dim3(256), 0, s, true, (const uint8_t*)m->embd,
-                           m->rs_h, H, c.vocab, (const int*)m->tokens, m->h, ds->status),
+                           m->rs_h, H, m->cf.vocab, (const int*)m->tokens, m->h, ds->status),
                   "embed launch");
+    // row-split projections: every rank's partial product, the residual added
+    // once (rank 0), then summed over the ranks
+    float* resid = m->rank == 0 ? m->h : nullptr;
     for (int l = 0; l < c.n_layers; l++) {
         Layer& Ly = m->L[l];
         // Q, K, V (+ RoPE, KV append)
@@ -312,10 +358,11 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
         else rc = launch_attention<KV, 128>(m, M, l, s);
         if (rc) return rc;
         // O projection + residual
-        a = gemv_args(m, Ly.o, H, m->Nq, M, m->h, m->h);
+        a = gemv_args(m, Ly.o, H, m->Nq, M, resid, m->h);
         rc = plain == PRO_F32 ? gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s)
                               : gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, s);
         if (rc) return rc;
+        if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
         // gate | up
         a = gemv_args(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu);
         if (fuse) {
@@ -329,7 +376,7 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
         }
         if (rc) return rc;
         // down + residual
-        a = gemv_args(m, Ly.down, H, F, M, m->h, m->h);
+        a = gemv_args(m, Ly.down, H, F, M, resid, m->h);
         if (fuse) {
             a.src = m->gu;
             rc = gemv_launch_mt<PRO_SILU, EPI_STORE, float>(ds, a, s);
@@ -350,9 +397,13 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
             }
         }
         if (rc) return rc;
+        if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
     }
-    // final norm + LM head + greedy argmax + advance
+    // final norm + LM head + greedy argmax + advance (this rank's vocabulary
+    // slice; with tp > 1 the keys are reduced over the ranks before the advance)
     GemvArgs a = gemv_args(m, m->out_w, c.vocab, H, M, nullptr, m->logits);
+    a.idx_offset = m->rank * c.vocab;
+    a.no_advance = m->tp > 1;
     a.pos = m->pos;
     a.amax_key = m->amax_key;
     a.done = m->done;
@@ -370,7 +421,18 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
         rc = a32 ? gemv_launch_mt<PRO_F32, EPI_ARGMAX, float>(ds, a, s)
                  : gemv_launch_mt<PRO_Q8, EPI_ARGMAX, float>(ds, a, s);
     }
-    return rc;
+    if (rc || m->tp == 1) return rc;
+    const NcclApi* api = nccl_api();
+    if (!api) return AXQ8_ERR_UNSUPPORTED;
+    if ((rc = nccl_check(api->AllReduce(m->amax_key, m->amax_key, (size_t)M, ncclUint64, ncclMax,
+                                        m->comm, s),
+                         "axdec: argmax all-reduce")))
+        return rc;
+    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3(1), dim3(32), 0, s, true, m->amax_key, M,
+                           m->pos, m->tokens, (const int*)m->feed, (const int*)m->ctl,
+                           m->out_tokens, m->argmax),
+                  "argmax advance launch");
+    return AXQ8_OK;
 }
 
 // Instantiate (once per batch size) the graph of one decode step.  The first
@@ -459,7 +521,23 @@ int axdec_tensor_index(const axdec_config_t* c, const char* name) {
 
 int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     if (!cfg || !out) return fail(AXQ8_ERR_INVALID, "axdec_create: null argument");
-    const axdec_config_t c = *cfg;
+    const axdec_config_t cf = *cfg;
+    const int tp = cf.tp_size > 1 ? cf.tp_size : 1, rank = tp > 1 ? cf.tp_rank : 0;
+    if (rank < 0 || rank >= tp)
+        return fail(AXQ8_ERR_INVALID, "axdec_create: tp_rank %d outside [0, %d)", cf.tp_rank, tp);
+    if (cf.n_kv_heads <= 0 || cf.n_kv_heads % tp || cf.ffn % (QK * tp) || cf.vocab % tp)
+        return fail(AXQ8_ERR_INVALID,
+                    "axdec_create: tp_size %d must divide n_kv_heads (%d), ffn / 32 (%d) and "
+                    "vocab (%d)",
+                    tp, cf.n_kv_heads, cf.ffn / QK, cf.vocab);
+    // this rank's dimensions
+    axdec_config_t c = cf;
+    c.n_heads = cf.n_heads / tp;
+    c.n_kv_heads = cf.n_kv_heads / tp;
+    c.ffn = cf.ffn / tp;
+    c.vocab = cf.vocab / tp;
+    c.tp_size = tp;
+    c.tp_rank = rank;
     if (c.n_layers <= 0 || c.hidden <= 0 || c.ffn <= 0 || c.n_heads <= 0 || c.n_kv_heads <= 0 ||
         c.vocab <= 0 || c.max_batch <= 0 || c.max_ctx <= 0)
         return fail(AXQ8_ERR_INVALID, "axdec_create: non-positive dimension");
@@ -479,6 +557,11 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     if (!ds) return AXQ8_ERR_CUDA;
     axdec_model* m = new axdec_model();
     m->c = c;
+    m->cf = cf;
+    m->cf.tp_size = tp;
+    m->cf.tp_rank = rank;
+    m->tp = tp;
+    m->rank = rank;
     m->ds = ds;
     m->Nq = c.n_heads * c.head_dim;
     m->Nkv = c.n_kv_heads * c.head_dim;
@@ -499,7 +582,7 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     const int M = c.max_batch, H = c.hidden, F = c.ffn;
     const size_t kvsz = c.kv_fp32 ? 4 : 2;
     const int64_t pages = (int64_t)M * m->max_blocks;
-    m->embd = (uint8_t*)dalloc(m, (size_t)c.vocab * m->rs_h, &rc);
+    m->embd = (uint8_t*)dalloc(m, (size_t)cf.vocab * m->rs_h, &rc);   // replicated
     m->out_w = (uint8_t*)dalloc(m, (size_t)c.vocab * m->rs_h, &rc);
     m->out_norm = (float*)dalloc(m, sizeof(float) * H, &rc);
     m->L.resize(c.n_layers);
@@ -578,6 +661,10 @@ int axdec_destroy(axdec_model_t* m) {
     for (auto& kv : m->graphs)
         if (kv.second.exec) cudaGraphExecDestroy(kv.second.exec);
     if (m->cap_stream) cudaStreamDestroy(m->cap_stream);
+    if (m->comm) {
+        const NcclApi* api = nccl_api();
+        if (api) api->CommDestroy(m->comm);
+    }
     for (void* p : m->allocs) cudaFree(p);
     delete m;
     return AXQ8_OK;
@@ -614,12 +701,26 @@ int axdec_set_tensor(axdec_model_t* m, const char* name, const void* host, int g
                       "axdec_set_tensor: copy");
         return AXQ8_OK;
     }
-    if (ggml_type != 8 || rows != d.N || cols != d.K)
+    if (ggml_type != 8 || rows != d.src_N || cols != d.src_K)
         return fail(AXQ8_ERR_INVALID,
                     "axdec_set_tensor: '%s' must be Q8_0 [%lld, %lld] (got type %d [%lld, %lld])",
-                    name, (long long)d.N, (long long)d.K, ggml_type, (long long)rows,
+                    name, (long long)d.src_N, (long long)d.src_K, ggml_type, (long long)rows,
                     (long long)cols);
     if (!strcmp(name, "output.weight")) m->out_set = true;
+    // this rank's slice: rows src_row0.., whole 32-blocks from column src_col0
+    std::vector<uint8_t> slice;
+    if (d.N != d.src_N || d.K != d.src_K) {
+        const size_t row_bytes = (size_t)(d.K / QK) * Q8_0_BYTES;
+        slice.resize((size_t)d.N * row_bytes);
+        const uint8_t* src = static_cast<const uint8_t*>(host);
+        for (int64_t n = 0; n < d.N; n++)
+            memcpy(slice.data() + (size_t)n * row_bytes,
+                   src + ((size_t)(d.src_row0 + n) * (d.src_K / QK) + d.src_col0 / QK) * Q8_0_BYTES,
+                   row_bytes);
+        host = slice.data();
+        rows = d.N;
+        cols = d.K;
+    }
     const size_t bytes = (size_t)rows * (cols / QK) * Q8_0_BYTES;
     void* staging = nullptr;
     void* tmp = nullptr;
@@ -637,7 +738,8 @@ int axdec_set_tensor(axdec_model_t* m, const char* name, const void* host, int g
     if (rc) return rc;
     if (!m->out_set && !strcmp(name, "token_embd.weight")) {
         // tied LM head until output.weight arrives
-        AXQ8_CUDA_TRY(cudaMemcpy(m->out_w, m->embd, (size_t)m->c.vocab * m->rs_h,
+        AXQ8_CUDA_TRY(cudaMemcpy(m->out_w, m->embd + (size_t)m->rank * m->c.vocab * m->rs_h,
+                                 (size_t)m->c.vocab * m->rs_h,
                                  cudaMemcpyDeviceToDevice),
                       "axdec_set_tensor: tie lm head");
     }
@@ -659,16 +761,18 @@ int axdec_init_random(axdec_model_t* m, uint64_t seed, float stdv) {
             AXQ8_CUDA_TRY(cudaGetLastError(), "axdec_init_random: fill");
             continue;
         }
+        // this rank's slice of the tensor axq8_synth_q8_0(sd, src_N, src_K) generates
         const uint64_t sd = seed + (uint64_t)axdec_tensor_index(&c, n.c_str());
         if (!d.rope_perm) {
-            rc = axq8_synth_q8_0(sd, d.N, d.K, 0.0f, stdv, 1, d.rows + d.row0 * q8r_row_stride(d.K),
-                                 nullptr);
+            rc = synth_q8_0_slice(sd, d.N, d.K, d.src_row0, d.src_col0, d.src_K, 0.0f, stdv,
+                                  d.rows + d.row0 * q8r_row_stride(d.K), nullptr);
             if (rc) return rc;
             continue;
         }
         void* tmp = nullptr;
         AXQ8_CUDA_TRY(cudaMalloc(&tmp, (size_t)d.N * q8r_row_stride(d.K)), "axdec_init_random: tmp");
-        rc = axq8_synth_q8_0(sd, d.N, d.K, 0.0f, stdv, 1, tmp, nullptr);
+        rc = synth_q8_0_slice(sd, d.N, d.K, d.src_row0, d.src_col0, d.src_K, 0.0f, stdv, tmp,
+                              nullptr);
         if (rc == AXQ8_OK) rc = place_rows(m, d, (const uint8_t*)tmp);
         cudaFree(tmp);
         if (rc) return rc;
@@ -687,6 +791,8 @@ int axdec_generate(axdec_model_t* m, const int32_t* prompts, int32_t n_seq, int3
     if (n_prompt + n_new - 1 > m->c.max_ctx)
         return fail(AXQ8_ERR_INVALID, "axdec_generate: %d positions exceed max_ctx %d",
                     n_prompt + n_new - 1, m->c.max_ctx);
+    if (m->tp > 1 && !m->comm)
+        return fail(AXQ8_ERR_STATE, "axdec_generate: tensor-parallel model not connected");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaGraphExec_t g;
     int rc = get_graph(m, n_seq, &g);
@@ -728,6 +834,8 @@ int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t
     if (n_seq <= 0 || n_seq > m->c.max_batch || n_prompt <= 0 || n_steps < n_prompt ||
         n_steps > m->c.max_ctx)
         return fail(AXQ8_ERR_INVALID, "axdec_forced: bad sizes");
+    if (m->tp > 1 && !m->comm)
+        return fail(AXQ8_ERR_STATE, "axdec_forced: tensor-parallel model not connected");
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     cudaGraphExec_t g;
     int rc = get_graph(m, n_seq, &g);
@@ -744,6 +852,30 @@ int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t
     }
     AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec: forced");
     return AXQ8_OK;
+}
+
+int axdec_tp_unique_id(void* id_out, int64_t id_bytes) {
+    if (!id_out || id_bytes < (int64_t)sizeof(ncclUniqueId))
+        return fail(AXQ8_ERR_INVALID, "axdec_tp_unique_id: needs %zu bytes", sizeof(ncclUniqueId));
+    const NcclApi* api = nccl_api();
+    if (!api) return AXQ8_ERR_UNSUPPORTED;
+    ncclUniqueId id;
+    int rc = nccl_check(api->GetUniqueId(&id), "ncclGetUniqueId");
+    if (rc) return rc;
+    memcpy(id_out, &id, sizeof(id));
+    return AXQ8_OK;
+}
+
+int axdec_tp_connect(axdec_model_t* m, const void* id) {
+    if (!m || !id) return fail(AXQ8_ERR_INVALID, "axdec_tp_connect: null argument");
+    if (m->tp == 1) return AXQ8_OK;
+    if (m->comm) return fail(AXQ8_ERR_STATE, "axdec_tp_connect: already connected");
+    const NcclApi* api = nccl_api();
+    if (!api) return AXQ8_ERR_UNSUPPORTED;
+    AXQ8_CUDA_TRY(cudaSetDevice(m->ds->device), "axdec_tp_connect: set device");
+    ncclUniqueId uid;
+    memcpy(&uid, id, sizeof(uid));
+    return nccl_check(api->CommInitRank(&m->comm, m->tp, uid, m->rank), "ncclCommInitRank");
 }
 
 }  // extern "C"

@@ -86,6 +86,8 @@ struct GemvArgs {
     const int* ctl;                // {n_prompt, feed_len, max_out}
     int* out_tokens;               // [M][max_out]
     int* argmax_out;               // [M]
+    int idx_offset;                // vocabulary index of row 0 (tensor-parallel LM head slice)
+    int no_advance;                // 1: leave the keys for a cross-rank reduction, no advance
 };
 
 constexpr int kGemvWarps = 16;                 // warps per CTA
@@ -289,7 +291,7 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, int m, int64_t n, bo
         float v = r ? v1 : v0;
         if (a.residual) v += a.residual[(int64_t)m * a.ldy + n + r];
         a.y[(int64_t)m * a.ldy + n + r] = v;
-        if (EPI == EPI_ARGMAX) atomicMax(keys + m, argmax_key(v, (int)(n + r)));
+        if (EPI == EPI_ARGMAX) atomicMax(keys + m, argmax_key(v, (int)(n + r) + a.idx_offset));
     }
 }
 
@@ -408,6 +410,10 @@ __device__ __forceinline__ void argmax_tail(const GemvArgs& a, const unsigned lo
     __syncthreads();
     if (!last) return;
     __threadfence();
+    if (a.no_advance) {     // the keys go to a cross-rank max first (argmax_advance_kernel)
+        if (threadIdx.x == 0) *a.done = 0;
+        return;
+    }
     if (threadIdx.x == 0) {
         const int n_prompt = a.ctl[0], feed_len = a.ctl[1], max_out = a.ctl[2];
         for (int m = 0; m < a.M; m++) {

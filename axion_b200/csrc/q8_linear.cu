@@ -173,8 +173,12 @@ __device__ inline float synth_value(uint64_t seed, uint64_t i, float mean, float
 }
 
 // layout 0: GGUF blocks (34 bytes each, row-major); layout 1: Q8R rows.
-__global__ void synth_q8_0_kernel(uint64_t seed, int64_t N, int64_t K, float mean, float stdv,
-                                  int layout, uint8_t* __restrict__ out) {
+// Rows [row0, row0 + N) and columns [col0, col0 + K) of a synthetic
+// [*, Kfull] tensor: element (r, k) is value number r * Kfull + k of the
+// generator, so a slice holds exactly the blocks of the whole tensor.
+__global__ void synth_q8_0_kernel(uint64_t seed, int64_t N, int64_t K, int64_t row0, int64_t col0,
+                                  int64_t Kfull, float mean, float stdv, int layout,
+                                  uint8_t* __restrict__ out) {
     const int64_t nb = K / QK;
     const int64_t rs = q8r_row_stride(K);
     for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < N * nb;
@@ -184,7 +188,7 @@ __global__ void synth_q8_0_kernel(uint64_t seed, int64_t N, int64_t K, float mea
         float amax = 0.0f;
 #pragma unroll
         for (int i = 0; i < QK; i++) {
-            v[i] = synth_value(seed, (uint64_t)(n * K + b * QK + i), mean, stdv);
+            v[i] = synth_value(seed, (uint64_t)((row0 + n) * Kfull + col0 + b * QK + i), mean, stdv);
             amax = fmaxf(amax, fabsf(v[i]));
         }
         const float d = __fdiv_rn(amax, 127.0f);
@@ -477,10 +481,26 @@ int axq8_synth_q8_0(uint64_t seed, int64_t N, int64_t K, float mean, float stdv,
     DeviceState* ds = device_state();
     if (!ds) return AXQ8_ERR_CUDA;
     synth_q8_0_kernel<<<grid_for(ds, N * (K / QK), 128), 128, 0,
-                        static_cast<cudaStream_t>(stream)>>>(seed, N, K, mean, stdv, layout,
-                                                             static_cast<uint8_t*>(out));
+                        static_cast<cudaStream_t>(stream)>>>(seed, N, K, 0, 0, K, mean, stdv,
+                                                             layout, static_cast<uint8_t*>(out));
     AXQ8_CUDA_TRY(cudaGetLastError(), "synth_q8_0_kernel launch");
     return AXQ8_OK;
 }
 
 }  // extern "C"
+
+namespace axq8 {
+
+int synth_q8_0_slice(uint64_t seed, int64_t N, int64_t K, int64_t row0, int64_t col0,
+                     int64_t Kfull, float mean, float stdv, void* rows, cudaStream_t stream) {
+    if (!rows || N <= 0 || K <= 0 || K % QK || col0 % QK || col0 + K > Kfull || row0 < 0)
+        return fail(AXQ8_ERR_INVALID, "synth slice: bad argument");
+    DeviceState* ds = device_state();
+    if (!ds) return AXQ8_ERR_CUDA;
+    synth_q8_0_kernel<<<grid_for(ds, N * (K / QK), 128), 128, 0, stream>>>(
+        seed, N, K, row0, col0, Kfull, mean, stdv, 1, static_cast<uint8_t*>(rows));
+    AXQ8_CUDA_TRY(cudaGetLastError(), "synth_q8_0_kernel launch");
+    return AXQ8_OK;
+}
+
+}  // namespace axq8

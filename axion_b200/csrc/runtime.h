@@ -37,6 +37,12 @@ DeviceState* device_state();
 // Synchronizes the device before replacing a smaller buffer.
 void* workspace(DeviceState* ds, size_t bytes);
 
+// Synthetic Q8_0 weight slice in the repacked row layout: rows [row0,
+// row0 + N) and columns [col0, col0 + K) of the [*, Kfull] tensor that
+// axq8_synth_q8_0(seed, ..., Kfull, ...) generates (q8_linear.cu).
+int synth_q8_0_slice(uint64_t seed, int64_t N, int64_t K, int64_t row0, int64_t col0,
+                     int64_t Kfull, float mean, float stdv, void* rows, cudaStream_t stream);
+
 #define AXQ8_CUDA_TRY(expr, what)                          \
     do {                                                    \
         cudaError_t _e = (expr);                            \

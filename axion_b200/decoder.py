@@ -34,13 +34,20 @@ class DecoderConfig:
     kv_block: int = 16
     act_mode: str = "q8"         # "q8" (A8, decode default) or "f32" (reference arithmetic)
     kv_fp32: bool = False        # fp16 KV pages by default
+    tp_size: int = 1             # tensor-parallel ranks (one process per GPU)
+    tp_rank: int = 0
 
     def c(self) -> _lib.axdec_config_t:
         return _lib.axdec_config_t(
             self.n_layers, self.hidden, self.ffn, self.n_heads, self.n_kv_heads, self.head_dim,
             self.vocab, self.rope_theta, self.rms_eps, self.max_batch, self.max_ctx,
             self.kv_block, _lib.AXQ8_ACT_Q8 if self.act_mode == "q8" else _lib.AXQ8_ACT_F32,
-            1 if self.kv_fp32 else 0)
+            1 if self.kv_fp32 else 0, self.tp_size, self.tp_rank)
+
+    @property
+    def vocab_local(self) -> int:
+        """Vocabulary rows of this rank's LM-head slice (logits width)."""
+        return self.vocab // max(1, self.tp_size)
 
 
 def config_from_gguf(g: GGUFLoader, **kw) -> DecoderConfig:
@@ -110,6 +117,22 @@ class Decoder:
     def weight_bytes_per_step(self) -> int:
         return self.lib.axdec_weight_bytes_per_step(self.h)
 
+    # -- tensor parallelism ---------------------------------------------------------
+    def tp_connect(self, group=None) -> None:
+        """Join the tensor-parallel communicator: rank 0 draws the NCCL id,
+        every rank of `group` (torch.distributed, any backend) receives it and
+        connects.  Collective over the tp_size ranks."""
+        if self.cfg.tp_size <= 1:
+            return
+        uid = share_tp_id(self.cfg.tp_rank, self._new_id, group)
+        buf = (C.c_ubyte * len(uid)).from_buffer_copy(uid)
+        check(self.lib.axdec_tp_connect(self.h, C.cast(buf, C.c_void_p)))
+
+    def _new_id(self) -> bytes:
+        buf = (C.c_ubyte * 128)()
+        check(self.lib.axdec_tp_unique_id(C.cast(buf, C.c_void_p), 128))
+        return bytes(buf)
+
     def step_kernels(self, n_seq: int = 1) -> int:
         """Kernels one decode step of n_seq sequences launches (-1 before the
         first generate/forced call with that n_seq)."""
@@ -123,7 +146,7 @@ class Decoder:
         p = np.ascontiguousarray(np.atleast_2d(np.asarray(prompts, np.int32)))
         n_seq, n_prompt = p.shape
         out = np.empty((n_seq, n_new), np.int32)
-        lg = np.empty((n_new, n_seq, self.cfg.vocab), np.float32) if logits else None
+        lg = np.empty((n_new, n_seq, self.cfg.vocab_local), np.float32) if logits else None
         ms = C.c_float(0)
         check(self.lib.axdec_generate(
             self.h, p.ctypes.data_as(C.c_void_p), n_seq, n_prompt, n_new,
@@ -133,11 +156,25 @@ class Decoder:
         return out, lg, ms.value
 
     def forced(self, tokens, n_prompt: int, stream=None) -> np.ndarray:
-        """Teacher-forced logits [n_steps - n_prompt + 1, n_seq, vocab]."""
+        """Teacher-forced logits [n_steps - n_prompt + 1, n_seq, vocab] (this
+        rank's vocabulary slice under tensor parallelism)."""
         t = np.ascontiguousarray(np.atleast_2d(np.asarray(tokens, np.int32)))
         n_seq, n_steps = t.shape
-        lg = np.empty((n_steps - n_prompt + 1, n_seq, self.cfg.vocab), np.float32)
+        lg = np.empty((n_steps - n_prompt + 1, n_seq, self.cfg.vocab_local), np.float32)
         check(self.lib.axdec_forced(self.h, t.ctypes.data_as(C.c_void_p), n_seq, n_prompt,
                                     n_steps, lg.ctypes.data_as(C.c_void_p),
                                     C.c_void_p(stream) if stream else None))
         return lg
+
+
+def share_tp_id(rank: int, make_id, group=None) -> bytes:
+    """The communicator id of rank 0, on every rank of `group`: rank 0 calls
+    make_id(), the bytes travel by a torch.distributed object broadcast."""
+    import torch.distributed as dist
+    obj = [make_id() if rank == 0 else None]
+    src = 0 if group is None else dist.get_global_rank(group, 0)
+    dist.broadcast_object_list(obj, src=src, group=group)
+    uid = obj[0]
+    if not isinstance(uid, (bytes, bytearray)) or len(uid) != 128:
+        raise RuntimeError("tensor-parallel id exchange failed")
+    return bytes(uid)

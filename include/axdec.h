@@ -42,6 +42,13 @@ typedef struct axdec_config {
     int32_t kv_block;     /* tokens per KV page, power of two (16) */
     int32_t act_mode;     /* AXQ8_ACT_Q8 (decode default) or AXQ8_ACT_F32 */
     int32_t kv_fp32;      /* 0: fp16 KV pages (default), 1: fp32 pages */
+    /* Tensor parallelism over tp_size GPUs (0 or 1: none), this model being
+     * rank tp_rank: Q, K, V, gate and up split by output rows (whole heads),
+     * O and down by input columns, the LM head by vocabulary; the embedding
+     * and norms are replicated.  Needs n_kv_heads, ffn / 32 and vocab
+     * divisible by tp_size. */
+    int32_t tp_size;
+    int32_t tp_rank;
 } axdec_config_t;
 
 typedef struct axdec_model axdec_model_t;
@@ -91,9 +98,21 @@ int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t
 /* Bytes of device memory the model holds (weights + KV pages + buffers). */
 int64_t axdec_device_bytes(const axdec_model_t* m);
 
-/* Bytes of Q8_0 weight streamed by one decode step (all linears + LM head,
+/* Bytes of Q8_0 weight streamed by one decode step on this rank (all linears + LM head,
  * at 34 bytes per 32 weights) — the algorithmic weight traffic per token. */
 int64_t axdec_weight_bytes_per_step(const axdec_model_t* m);
+
+/* Tensor-parallel set-up.  Rank 0 draws a communicator id (128 bytes,
+ * written to id_out) and every rank passes the same id to axdec_tp_connect
+ * (collectively: all tp_size ranks call it).  The step then sums the partial
+ * hidden states after the O and down projections with an NCCL all-reduce
+ * over NVLink and takes the greedy token as a max all-reduce of packed
+ * (logit, index) keys.  With tp_size > 1, logits_out of axdec_generate /
+ * axdec_forced receives this rank's vocabulary slice ([steps][n_seq][vocab /
+ * tp_size], vocabulary rows tp_rank * vocab / tp_size onwards).  NCCL is
+ * loaded at run time; AXQ8_ERR_UNSUPPORTED when it cannot be found. */
+int axdec_tp_unique_id(void* id_out, int64_t id_bytes);
+int axdec_tp_connect(axdec_model_t* m, const void* id);
 
 /* Kernels launched by one decode step of n_seq sequences: the kernel nodes
  * of the step's CUDA graph, captured by the first axdec_generate/axdec_forced

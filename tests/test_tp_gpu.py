@@ -1,0 +1,128 @@
+"""Tensor-parallel decode (include/axdec.h tp_size / tp_rank) against the
+single-GPU decoder: 2 (and 4) ranks as child processes, one GPU each, the
+decoder's own NCCL communicator for the hidden-state and argmax
+all-reduces.  Skipped with fewer GPUs than ranks.
+
+* A32 + fp32 KV on the tiny golden model: the only difference is the order
+  of the fp32 sums (per-rank partial products, then the all-reduce), so the
+  logits agree to 1e-4 of the step's largest |logit| and the greedy tokens
+  are equal.
+* A8 + fp16 KV (decode default): a last-bit difference in the hidden state
+  can move one activation across a quantization boundary, so the tolerance
+  and token check are those of the single-GPU A8 tests.
+* TinyLlama architecture at full size with device-generated weights: every
+  rank generates exactly its slice of the single-GPU tensors.
+"""
+from __future__ import annotations
+
+import socket
+
+import numpy as np
+import pytest
+
+from conftest import golden
+
+pytestmark = pytest.mark.gpu
+
+TP_F32_TOL = 1e-4
+A8_TOL = 5e-2
+
+
+def _port() -> int:
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _need(world: int):
+    import torch
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+
+
+def _rel(a, b) -> float:
+    a = a.reshape(a.shape[0], -1).astype(np.float64)
+    b = b.reshape(b.shape[0], -1).astype(np.float64)
+    return float(np.max(np.max(np.abs(a - b), axis=1) / np.max(np.abs(b), axis=1)))
+
+
+def _top1_consistent(lg, ref, tol) -> bool:
+    for a, r in zip(lg.reshape(lg.shape[0], -1), ref.reshape(ref.shape[0], -1)):
+        ia, ir = int(np.argmax(a)), int(np.argmax(r))
+        if ia != ir and abs(r[ia] - r[ir]) > tol * np.max(np.abs(r)):
+            return False
+    return True
+
+
+def _run(fn, world, *args):
+    import torch.multiprocessing as mp
+    mp.spawn(fn, args=(world, _port()) + args, nprocs=world, join=True)
+
+
+def _gather(out, world):
+    toks = [np.load(out / f"tok{r}.npy") for r in range(world)]
+    lgs = [np.load(out / f"lg{r}.npy") for r in range(world)]
+    for t in toks[1:]:
+        assert np.array_equal(t, toks[0])          # every rank advances the same tokens
+    return toks[0], np.concatenate(lgs, axis=-1)   # vocabulary slices in rank order
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_f32_matches_single_gpu(cuda, tmp_path, world):
+    _need(world)
+    import _tp_worker
+    from axion_b200.decoder import Decoder
+    if world == 4:
+        pytest.skip("tiny golden model has 2 KV heads")
+    prompt = golden("tiny_llama_ref.npz")["prompt"].tolist()
+    ref = Decoder.from_gguf(golden("tiny_llama.gguf"), act_mode="f32", kv_fp32=True, max_ctx=32)
+    rt, rl, _ = ref.generate(prompt, 12, logits=True)
+    ref.close()
+    _run(_tp_worker.tiny_gguf, world, str(tmp_path), str(golden("tiny_llama.gguf")), "f32", True,
+         prompt, 12)
+    toks, lg = _gather(tmp_path, world)
+    assert np.array_equal(toks, rt)
+    assert _rel(lg[:, 0, :], rl[:, 0, :]) <= TP_F32_TOL
+
+
+def test_tp_q8_matches_single_gpu(cuda, tmp_path):
+    _need(2)
+    import _tp_worker
+    from axion_b200.decoder import Decoder
+    prompt = golden("tiny_llama_ref.npz")["prompt"].tolist()
+    ref = Decoder.from_gguf(golden("tiny_llama.gguf"), act_mode="q8", kv_fp32=False, max_ctx=32)
+    rt, rl, _ = ref.generate(prompt, 12, logits=True)
+    ref.close()
+    _run(_tp_worker.tiny_gguf, 2, str(tmp_path), str(golden("tiny_llama.gguf")), "q8", False,
+         prompt, 12)
+    toks, lg = _gather(tmp_path, 2)
+    assert _rel(lg[:1, 0, :], rl[:1, 0, :]) <= 1e-3
+    assert _rel(lg[:, 0, :], rl[:, 0, :]) <= A8_TOL
+    assert _top1_consistent(lg[:, 0, :], rl[:, 0, :], A8_TOL)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_tinyllama_architecture_batch(cuda, tmp_path, world):
+    """Full-size TinyLlama architecture (4 KV heads), batch of 3, device
+    weights: rank slices of the generator reproduce the single-GPU model."""
+    _need(world)
+    import _tp_worker
+    from axion_b200.decoder import Decoder, DecoderConfig
+    kw = dict(n_layers=22, hidden=2048, ffn=5632, n_heads=32, n_kv_heads=4, head_dim=64,
+              vocab=32000, rope_theta=10000.0, rms_eps=1e-5, max_batch=3, max_ctx=64)
+    prompts = np.random.default_rng(4).integers(0, 32000, (3, 6)).astype(np.int32)
+    ref = Decoder(DecoderConfig(**kw))
+    ref.init_random(0xA710, std=0.02)
+    rt, rl, _ = ref.generate(prompts, 4, logits=True)
+    ref.close()
+    _run(_tp_worker.synthetic, world, str(tmp_path), kw, 0xA710, prompts.tolist(), 4)
+    toks, lg = _gather(tmp_path, world)
+    err = _rel(lg.reshape(4, -1), rl.reshape(4, -1))
+    print(f"tp{world} tinyllama-arch A8 logits rel err vs 1 GPU: {err:.2e}")
+    # 22 layers x 6 prompt positions of A8 re-quantization already separate
+    # the first generated step by ~2e-2 (as against the oracle on one GPU)
+    assert err <= A8_TOL
+    for b in range(3):
+        assert _top1_consistent(lg[:, b, :], rl[:, b, :], A8_TOL)
