@@ -50,10 +50,12 @@ __global__ void embed_kernel(const uint8_t* __restrict__ rows, int64_t rs, int H
 // One CTA per row.  out = (x * (1/sqrt(mean(x^2) + eps))) * w with the
 // reference's separately rounded operations; the sum of squares is a fixed
 // tree (warp sums, then warps in order), not the reference's sequential sum.
+// dxt > 0: the block scales go transposed, dx[b * dxt + m] (the tensor-core
+// product's layout), else row-major dx[m * H/32 + b].  Same below.
 template <bool Q8>
 __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int H,
                                float eps, float* __restrict__ out, int8_t* __restrict__ xq,
-                               float* __restrict__ dx) {
+                               float* __restrict__ dx, int dxt) {
     __shared__ float red[32];
     pdl_launch_dependents();
     pdl_wait();
@@ -81,7 +83,8 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
         for (int b = warp; b < nb; b += nw) {
             const int k = b * QK + lane;
             const float v = __fmul_rn(__fmul_rn(xr[k], inv), w[k]);
-            quant_block_warp(v, lane, xq + (int64_t)m * H + b * QK, dx + (int64_t)m * nb + b);
+            quant_block_warp(v, lane, xq + (int64_t)m * H + b * QK,
+                             dx + (dxt ? (int64_t)b * dxt + m : (int64_t)m * nb + b));
         }
     }
 }
@@ -121,7 +124,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
                                    int max_blocks, int n_heads, int n_kv, int bps, int cp,
                                    float scale, float* __restrict__ part, int* __restrict__ counters,
                                    float* __restrict__ out, int8_t* __restrict__ xq,
-                                   float* __restrict__ dx) {
+                                   float* __restrict__ dx, int dxt) {
     constexpr int B = 16;
     constexpr int DL = HD / 32;            // dims per lane in the value accumulation
     constexpr int V16 = 16 / sizeof(KV);    // cache elements per 16-byte copy
@@ -273,13 +276,101 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
     const float id = am == 0.0f ? 0.0f : __fdiv_rn(127.0f, am);
 #pragma unroll
     for (int i = 0; i < DL; i++) xq[base + i] = (int8_t)q8_round(__fmul_rn(v[i], id));
-    if ((lane % (32 / DL)) == 0) dx[base / QK] = __fdiv_rn(am, 127.0f);
+    if ((lane % (32 / DL)) == 0) {
+        const int64_t col = (int64_t)h * HD + lane * DL;   // position in the row of n_heads*HD
+        dx[dxt ? (col / QK) * dxt + m : base / QK] = __fdiv_rn(am, 127.0f);
+    }
+}
+
+// ---- RoPE + KV append over product rows (wide batches) ---------------------------
+// The tensor-core product writes qkv [M][Nq + 2 Nkv] with the Q and K rows of
+// each head in the (j, j + hd/2) pair order of the permuted weight.  One warp
+// per (sequence, head): it reads the whole head, then rotates Q back into
+// natural order in place and writes K (rotated) and V into the KV page of the
+// sequence's position, as the GEMV's RoPE/KV epilogue does.
+template <typename KV>
+__global__ void rope_kv_rows_kernel(float* __restrict__ qkv, int M, int n_heads, int n_kv, int hd,
+                                   const int* __restrict__ pos, const float2* __restrict__ rope,
+                                   int max_ctx, const int* __restrict__ block_table, int max_blocks,
+                                   int B, KV* __restrict__ kc, KV* __restrict__ vc,
+                                   int* __restrict__ status) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int lane = threadIdx.x & 31;
+    const int heads = n_heads + 2 * n_kv;
+    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    if (gw >= M * heads) return;
+    const int m = gw / heads, hh = gw % heads;
+    const int half = hd / 2;
+    const int p = pos[m];
+    if (p < 0 || p >= max_ctx) {
+        if (lane == 0) record_status(status, AXQ8_ERR_INVALID);
+        return;
+    }
+    const int page = block_table[m * max_blocks + p / B], slot = p % B;
+    const int ldq = (n_heads + 2 * n_kv) * hd;
+    float* row = qkv + (int64_t)m * ldq + (int64_t)hh * hd;
+    if (hh >= n_heads + n_kv) {                       // V: natural order, copy
+        KV* dst = vc + (((int64_t)page * n_kv + (hh - n_heads - n_kv)) * B + slot) * hd;
+        for (int d = lane; d < hd; d += 32) kv_store(dst + d, row[d]);
+        return;
+    }
+    // pairs j = lane, lane + 32 (hd <= 128)
+    float v0[2], v1[2];
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int j = lane + 32 * t;
+        if (j < half) {
+            v0[t] = row[2 * j];
+            v1[t] = row[2 * j + 1];
+        }
+    }
+    __syncwarp();
+    const bool isk = hh >= n_heads;
+    KV* kdst = isk ? kc + (((int64_t)page * n_kv + (hh - n_heads)) * B + slot) * hd : nullptr;
+#pragma unroll
+    for (int t = 0; t < 2; t++) {
+        const int j = lane + 32 * t;
+        if (j >= half) continue;
+        const float2 cs = rope[(int64_t)p * half + j];
+        const float r0 = __fsub_rn(__fmul_rn(v0[t], cs.x), __fmul_rn(v1[t], cs.y));
+        const float r1 = __fadd_rn(__fmul_rn(v0[t], cs.y), __fmul_rn(v1[t], cs.x));
+        if (!isk) {
+            row[j] = r0;
+            row[j + half] = r1;
+        } else {
+            kv_store(kdst + j, r0);
+            kv_store(kdst + j + half, r1);
+        }
+    }
+}
+
+// ---- greedy argmax over logit rows (wide batches) ---------------------------------
+// Grid (chunks, M): each CTA folds its part of row m into amax_key[m] (zero
+// before; argmax_advance_kernel consumes and clears it).
+__global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int idx_offset,
+                                   unsigned long long* __restrict__ amax_key) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int m = blockIdx.y;
+    const float* row = logits + (int64_t)m * V;
+    unsigned long long best = 0ull;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
+        const unsigned long long k = argmax_key(row[i], i + idx_offset);
+        best = k > best ? k : best;
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+        best = t > best ? t : best;
+    }
+    if ((threadIdx.x & 31) == 0 && best) atomicMax(amax_key + m, best);
 }
 
 // ---- greedy step advance after a cross-rank argmax ------------------------------
-// The tensor-parallel LM head leaves each sequence's packed (logit, global
-// index) key in amax_key; after the max all-reduce over ranks one thread
-// performs the advance of the single-GPU argmax epilogue: record the token,
+// The tensor-parallel LM head (and the wide-batch argmax) leave each
+// sequence's packed (logit, global index) key in amax_key; after the max
+// all-reduce over ranks one thread performs the advance of the argmax epilogue: record the token,
 // feed the next input (prompt token or the argmax), move the position, and
 // zero the key for the next step.
 __global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key, int M,
@@ -309,7 +400,7 @@ __global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key,
 template <bool Q8>
 __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
                                 float* __restrict__ out, int8_t* __restrict__ xq,
-                                float* __restrict__ dx) {
+                                float* __restrict__ dx, int dxt) {
     pdl_launch_dependents();
     pdl_wait();
     const int nb = F / QK;
@@ -324,7 +415,8 @@ __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
     if (!Q8) {
         out[(int64_t)m * F + i] = a;
     } else {
-        quant_block_warp(a, lane, xq + (int64_t)m * F + b * QK, dx + (int64_t)m * nb + b);
+        quant_block_warp(a, lane, xq + (int64_t)m * F + b * QK,
+                         dx + (dxt ? (int64_t)b * dxt + m : (int64_t)m * nb + b));
     }
 }
 

@@ -22,6 +22,7 @@
 #include <cuda_runtime.h>
 #include <math.h>
 #include <stdint.h>
+#include <stdlib.h>
 #include <string.h>
 
 #include <algorithm>
@@ -36,6 +37,7 @@
 #include "decode_ops.cuh"
 #include "nccl_dl.h"
 #include "q8_gemv.cuh"
+#include "q8_mma.h"
 #include "runtime.h"
 
 using namespace axq8;
@@ -98,6 +100,7 @@ struct axdec_model {
     unsigned long long* amax_key = nullptr;   // [M] argmax epilogue keys
     int* done = nullptr;                      // argmax epilogue completion counter
     int* attn_cnt = nullptr;                  // [M, n_kv] attention split counters
+    MmaScratch mma_sc;                        // split-K scratch of the wide-batch products
     cudaStream_t cap_stream = nullptr;
     std::map<int, Graph> graphs;  // per batch size
 };
@@ -275,7 +278,7 @@ GemvArgs gemv_args(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, in
 }
 
 template <typename KV, int HD>
-int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s) {
+int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s, int dxt) {
     const axdec_config_t& c = m->c;
     const int G = c.n_heads / c.n_kv_heads;
     // pages staged at once: up to 32 KB of K and V
@@ -291,27 +294,117 @@ int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s) {
                            (const float*)m->qkv, m->Nqkv, (const int*)m->pos, (const KV*)Ly.kc,
                            (const KV*)Ly.vc, (const int*)m->block_table, m->max_blocks, c.n_heads,
                            c.n_kv_heads, m->bps, cp, scale, m->part, m->attn_cnt, m->x32, m->xq,
-                           m->dx),
+                           m->dx, dxt),
                   "attention launch");
     return AXQ8_OK;
 }
 
-int launch_rmsnorm(axdec_model* m, int M, const float* x, const float* w, cudaStream_t s) {
+int launch_rmsnorm(axdec_model* m, int M, const float* x, const float* w, cudaStream_t s,
+                   int dxt = 0) {
     const axdec_config_t& c = m->c;
     if (c.act_mode == AXQ8_ACT_F32) {
         AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<false>, dim3(M), dim3(kNormThreads), 0, s, true, x, w,
-                               c.hidden, c.rms_eps, m->x32, (int8_t*)nullptr, (float*)nullptr),
+                               c.hidden, c.rms_eps, m->x32, (int8_t*)nullptr, (float*)nullptr, 0),
                       "rmsnorm launch");
     } else {
         AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<true>, dim3(M), dim3(kNormThreads), 0, s, true, x, w,
-                               c.hidden, c.rms_eps, (float*)nullptr, m->xq, m->dx),
+                               c.hidden, c.rms_eps, (float*)nullptr, m->xq, m->dx, dxt),
                       "rmsnorm launch");
     }
     return AXQ8_OK;
 }
 
+// Whether a step of M sequences runs wide: A8, M >= 32 and every linear
+// tiled by the tensor-core product.
+bool wide_step(const axdec_model* m, int M) {
+    // AXDEC_NARROW=1 keeps every batch on the GEMV step (comparison runs)
+    static const bool narrow = [] {
+        const char* e = getenv("AXDEC_NARROW");
+        return e && atoi(e) != 0;
+    }();
+    if (narrow) return false;
+    const axdec_config_t& c = m->c;
+    const int64_t H = c.hidden, F = c.ffn;
+    return c.act_mode == AXQ8_ACT_Q8 && M >= 32 && mma_shape_ok(m->Nqkv, H, M) &&
+           mma_shape_ok(H, m->Nq, M) && mma_shape_ok(2 * F, H, M) && mma_shape_ok(H, F, M) &&
+           mma_shape_ok(c.vocab, H, M);
+}
+
+int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
+                const float* resid, float* y, cudaStream_t s) {
+    axq8_weight_t w = {};
+    w.rows = const_cast<uint8_t*>(rows);
+    w.N = N;
+    w.K = K;
+    w.row_stride = q8r_row_stride(K);
+    w.device = m->ds->device;
+    return mma_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, nullptr, s, &m->mma_sc);
+}
+
+// Wide batches (M >= 32, prefill-like widths of batched decode): every linear
+// on the tensor cores (tcgen05 kind::i8) from A8 activations with transposed
+// block scales, the producers (RMSNorm, SiLU*up, attention) writing that
+// layout, RoPE + KV append and the greedy argmax as kernels of their own.
+template <typename KV>
+int launch_step_wide(axdec_model* m, int M, cudaStream_t s) {
+    const axdec_config_t& c = m->c;
+    const int H = c.hidden, F = c.ffn, hd = c.head_dim;
+    const int dxt = (int)mma_scale_pitch(M);
+    DeviceState* ds = m->ds;
+    int rc;
+    AXQ8_CUDA_TRY(launch_k(embed_kernel, dim3(M), dim3(256), 0, s, true, (const uint8_t*)m->embd,
+                           m->rs_h, H, m->cf.vocab, (const int*)m->tokens, m->h, ds->status),
+                  "embed launch");
+    float* resid = m->rank == 0 ? m->h : nullptr;
+    const int heads = c.n_heads + 2 * c.n_kv_heads;
+    for (int l = 0; l < c.n_layers; l++) {
+        Layer& Ly = m->L[l];
+        if ((rc = launch_rmsnorm(m, M, m->h, Ly.attn_norm, s, dxt))) return rc;
+        if ((rc = wide_linear(m, Ly.qkv, m->Nqkv, H, M, nullptr, m->qkv, s))) return rc;
+        AXQ8_CUDA_TRY(launch_k(rope_kv_rows_kernel<KV>, dim3((M * heads + 7) / 8), dim3(256), 0, s,
+                               true, m->qkv, M, c.n_heads, c.n_kv_heads, hd, (const int*)m->pos,
+                               (const float2*)m->rope, c.max_ctx, (const int*)m->block_table,
+                               m->max_blocks, c.kv_block, (KV*)Ly.kc, (KV*)Ly.vc, ds->status),
+                      "rope/kv launch");
+        if (hd == 32) rc = launch_attention<KV, 32>(m, M, l, s, dxt);
+        else if (hd == 64) rc = launch_attention<KV, 64>(m, M, l, s, dxt);
+        else rc = launch_attention<KV, 128>(m, M, l, s, dxt);
+        if (rc) return rc;
+        if ((rc = wide_linear(m, Ly.o, H, m->Nq, M, resid, m->h, s))) return rc;
+        if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
+        if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s, dxt))) return rc;
+        if ((rc = wide_linear(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu, s))) return rc;
+        const int nwarps = M * (F / QK);
+        AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0, s, true,
+                               (const float*)m->gu, F, M, (float*)nullptr, m->xq, m->dx, dxt),
+                      "silu launch");
+        if ((rc = wide_linear(m, Ly.down, H, F, M, resid, m->h, s))) return rc;
+        if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
+    }
+    if ((rc = launch_rmsnorm(m, M, m->h, m->out_norm, s, dxt))) return rc;
+    if ((rc = wide_linear(m, m->out_w, c.vocab, H, M, nullptr, m->logits, s))) return rc;
+    const int chunks = std::max(1, std::min(64, c.vocab / 4096));
+    AXQ8_CUDA_TRY(launch_k(argmax_rows_kernel, dim3(chunks, M), dim3(256), 0, s, true,
+                           (const float*)m->logits, c.vocab, m->rank * c.vocab, m->amax_key),
+                  "argmax launch");
+    if (m->tp > 1) {
+        const NcclApi* api = nccl_api();
+        if (!api) return AXQ8_ERR_UNSUPPORTED;
+        if ((rc = nccl_check(api->AllReduce(m->amax_key, m->amax_key, (size_t)M, ncclUint64, ncclMax,
+                                            m->comm, s),
+                             "axdec: argmax all-reduce")))
+            return rc;
+    }
+    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3(1), dim3(32), 0, s, true, m->amax_key, M,
+                           m->pos, m->tokens, (const int*)m->feed, (const int*)m->ctl,
+                           m->out_tokens, m->argmax),
+                  "argmax advance launch");
+    return AXQ8_OK;
+}
+
 template <typename KV>
 int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
+    if (wide_step(m, M)) return launch_step_wide<KV>(m, M, s);
     const axdec_config_t& c = m->c;
     const int H = c.hidden, F = c.ffn, hd = c.head_dim;
     const bool a32 = c.act_mode == AXQ8_ACT_F32;
@@ -353,9 +446,9 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
         }
         if (rc) return rc;
         // attention (+ split merge, + Q8 of its output)
-        if (hd == 32) rc = launch_attention<KV, 32>(m, M, l, s);
-        else if (hd == 64) rc = launch_attention<KV, 64>(m, M, l, s);
-        else rc = launch_attention<KV, 128>(m, M, l, s);
+        if (hd == 32) rc = launch_attention<KV, 32>(m, M, l, s, 0);
+        else if (hd == 64) rc = launch_attention<KV, 64>(m, M, l, s, 0);
+        else rc = launch_attention<KV, 128>(m, M, l, s, 0);
         if (rc) return rc;
         // O projection + residual
         a = gemv_args(m, Ly.o, H, m->Nq, M, resid, m->h);
@@ -385,13 +478,13 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
             if (a32) {
                 AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, dim3((nwarps + 7) / 8), dim3(256), 0,
                                        s, true, (const float*)m->gu, F, M, m->x32,
-                                       (int8_t*)nullptr, (float*)nullptr),
+                                       (int8_t*)nullptr, (float*)nullptr, 0),
                               "silu launch");
                 rc = gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s);
             } else {
                 AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0,
                                        s, true, (const float*)m->gu, F, M, (float*)nullptr, m->xq,
-                                       m->dx),
+                                       m->dx, 0),
                               "silu launch");
                 rc = gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, s);
             }
@@ -600,7 +693,8 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     const int maxK = std::max(std::max(H, F), m->Nq);
     m->h = (float*)dalloc(m, sizeof(float) * M * H, &rc);
     m->xq = (int8_t*)dalloc(m, (size_t)M * maxK, &rc);
-    m->dx = (float*)dalloc(m, sizeof(float) * M * (maxK / QK), &rc);
+    // block scales: [M][K/32], or transposed [K/32][M rounded up to 4] (wide steps)
+    m->dx = (float*)dalloc(m, sizeof(float) * mma_scale_pitch(M) * (maxK / QK), &rc);
     m->x32 = (float*)dalloc(m, sizeof(float) * M * maxK, &rc);
     m->qkv = (float*)dalloc(m, sizeof(float) * M * m->Nqkv, &rc);
     m->gu = (float*)dalloc(m, sizeof(float) * M * 2 * F, &rc);
@@ -617,6 +711,32 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->amax_key = (unsigned long long*)dalloc(m, sizeof(unsigned long long) * M, &rc);
     m->done = (int*)dalloc(m, sizeof(int), &rc);
     m->attn_cnt = (int*)dalloc(m, sizeof(int) * M * c.n_kv_heads, &rc);
+    if (rc == AXQ8_OK && c.act_mode == AXQ8_ACT_Q8 && M >= 32) {
+        // split-K scratch for every width a wide step may run at
+        size_t part = 0;
+        int64_t cnt = 0;
+        const int64_t shapes[5][2] = {{m->Nqkv, H}, {H, m->Nq}, {2 * (int64_t)F, H}, {H, F},
+                                      {c.vocab, H}};
+        for (int mm = 32; mm <= M; mm++)
+            for (auto& sh : shapes) {
+                if (!mma_shape_ok(sh[0], sh[1], mm)) continue;
+                size_t pb;
+                int64_t cn;
+                mma_split_needs(ds, sh[0], sh[1], mm, &pb, &cn);
+                part = std::max(part, pb);
+                cnt = std::max(cnt, cn);
+            }
+        if (part) {
+            m->mma_sc.part = (float*)dalloc(m, part, &rc);
+            m->mma_sc.part_bytes = part;
+            m->mma_sc.counters = (int*)dalloc(m, sizeof(int) * cnt, &rc);
+            m->mma_sc.counter_slots = cnt;
+            if (rc == AXQ8_OK) {
+                cudaError_t e = cudaMemset(m->mma_sc.counters, 0, sizeof(int) * cnt);
+                if (e != cudaSuccess) rc = cuda_fail(e, "axdec: split counters");
+            }
+        }
+    }
     if (rc == AXQ8_OK) {
         cudaError_t e = cudaStreamCreateWithFlags(&m->cap_stream, cudaStreamNonBlocking);
         if (e != cudaSuccess) rc = cuda_fail(e, "axdec: stream create");

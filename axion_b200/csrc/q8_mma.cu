@@ -113,22 +113,48 @@ bool mma_eligible(const axq8_weight_t* w, int64_t M) {
            w->K >= kMmaKC && w->K % kMmaKC == 0 && w->K <= (1 << 20);
 }
 
+namespace {
+// Tile sizes and split count of one call.
+struct MmaPlan {
+    int BN, splits, per;
+    int64_t tiles_n, tiles_m, tiles;
+};
+MmaPlan mma_plan(DeviceState* ds, int64_t N, int64_t K, int64_t M, bool dots) {
+    MmaPlan p;
+    p.BN = M >= 128 ? 128 : (M >= 64 ? 64 : 32);
+    p.tiles_n = (N + kMmaBM - 1) / kMmaBM;
+    p.tiles_m = (M + p.BN - 1) / p.BN;
+    p.tiles = p.tiles_n * p.tiles_m;
+    const int nst = (int)(K / kMmaKC);
+    const int64_t slots = (int64_t)ds->sm_count * (p.BN == 64 ? 2 : 1);
+    int splits = 1;
+    if (p.tiles < slots && !dots) {
+        splits = (int)std::min<int64_t>(slots / p.tiles, std::max(1, nst / 2));
+        splits = std::max(splits, 1);
+    }
+    p.per = (nst + splits - 1) / splits;
+    p.splits = (nst + p.per - 1) / p.per;
+    return p;
+}
+}  // namespace
+
+void mma_split_needs(DeviceState* ds, int64_t N, int64_t K, int64_t M, size_t* part_bytes,
+                     int64_t* counters) {
+    const MmaPlan p = mma_plan(ds, N, K, M, false);
+    *part_bytes = p.splits > 1 ? sizeof(float) * (size_t)p.splits * M * N : 0;
+    *counters = p.splits > 1 ? p.tiles : 0;
+}
+
 int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
                int64_t M, const float* residual, float* y, int64_t ldy, int32_t* dots,
-               cudaStream_t stream) {
+               cudaStream_t stream, const MmaScratch* scratch) {
     if (!w || M < 32 || w->N < kMmaBM || w->K % kMmaKC || !xq || !dxT || !y || ldy < w->N)
         return fail(AXQ8_ERR_INVALID, "tensor-core linear: unsupported arguments");
     if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(dxT) & 15))
         return fail(AXQ8_ERR_INVALID, "tensor-core linear: xq/dxT not 16-byte aligned");
     const int64_t N = w->N, K = w->K, Mp = mma_scale_pitch(M);
-    // activation rows per tile; AXQ8_MMA_BN (32/64/128) caps it for tuning
-    static const int bn_cap = [] {
-        const char* e = getenv("AXQ8_MMA_BN");
-        const int v = e ? atoi(e) : 128;
-        return v == 32 || v == 64 ? v : 128;
-    }();
-    int BN = M >= 128 ? 128 : (M >= 64 ? 64 : 32);
-    if (BN > bn_cap) BN = bn_cap;
+    const MmaPlan plan = mma_plan(ds, N, K, M, dots != nullptr);
+    const int BN = plan.BN;
     CUtensorMap tw, tx, td;
     int rc = make_map(&tw, CU_TENSOR_MAP_DATA_TYPE_UINT8, w->rows, K, N, w->row_stride, kMmaKC,
                       kMmaBM, CU_TENSOR_MAP_SWIZZLE_128B, "weight quants");
@@ -140,17 +166,8 @@ int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const 
                   CU_TENSOR_MAP_SWIZZLE_NONE, "activation scales");
     if (rc) return rc;
 
-    const int64_t tiles_n = (N + kMmaBM - 1) / kMmaBM, tiles_m = (M + BN - 1) / BN;
-    const int64_t tiles = tiles_n * tiles_m;
-    const int nst = (int)(K / kMmaKC);
-    const int64_t slots = (int64_t)ds->sm_count * (BN == 64 ? 2 : 1);
-    int splits = 1;
-    if (tiles < slots && !dots) {
-        splits = (int)std::min<int64_t>(slots / tiles, std::max(1, nst / 2));
-        splits = std::max(splits, 1);
-    }
-    const int per = (nst + splits - 1) / splits;
-    splits = (nst + per - 1) / per;
+    const int64_t tiles_n = plan.tiles_n, tiles_m = plan.tiles_m, tiles = plan.tiles;
+    const int splits = plan.splits, per = plan.per;
     if (tiles_n > 65535) return fail(AXQ8_ERR_UNSUPPORTED, "tensor-core linear: too many tiles");
 
     MmaArgs a = {};
@@ -166,10 +183,18 @@ int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const 
     a.dots = dots;
     a.status = ds->status;
     if (splits > 1) {
-        if (tiles > kCounterSlots)
-            return fail(AXQ8_ERR_UNSUPPORTED, "tensor-core linear: too many split tiles");
-        rc = split_scratch(ds, sizeof(float) * (size_t)splits * M * N, &a.part, &a.counters);
-        if (rc) return rc;
+        const size_t need = sizeof(float) * (size_t)splits * M * N;
+        if (scratch) {
+            if (scratch->part_bytes < need || scratch->counter_slots < tiles)
+                return fail(AXQ8_ERR_INVALID, "tensor-core linear: caller scratch too small");
+            a.part = scratch->part;
+            a.counters = scratch->counters;
+        } else {
+            if (tiles > kCounterSlots)
+                return fail(AXQ8_ERR_UNSUPPORTED, "tensor-core linear: too many split tiles");
+            rc = split_scratch(ds, need, &a.part, &a.counters);
+            if (rc) return rc;
+        }
     }
     const dim3 grid((unsigned)tiles_m, (unsigned)tiles_n, (unsigned)splits);
     if (dots) {

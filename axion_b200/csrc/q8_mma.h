@@ -18,13 +18,34 @@ constexpr int kMmaMinM = 32;
 // N >= 128, K a multiple of 128.
 bool mma_eligible(const axq8_weight_t* w, int64_t M);
 
+// Caller-owned split-K scratch (partials and per-tile counters, the counters
+// zero before first use); without it the library's per-device scratch is used
+// (allocated, and grown, on demand: not usable inside a graph capture).
+struct MmaScratch {
+    float* part = nullptr;
+    size_t part_bytes = 0;
+    int* counters = nullptr;
+    int64_t counter_slots = 0;
+};
+
 // y[M][ldy] = residual + xq . W^T with xq [M][K] int8 (16-byte aligned rows)
 // and the activation scales transposed, dxT [K/32][Mp] fp32 (Mp = M rounded
 // up to 4).  dots, when not null, receives every raw int32 block dot
 // [M][N][K/32].  Requires the shape part of mma_eligible (any M >= 32).
 int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
                int64_t M, const float* residual, float* y, int64_t ldy, int32_t* dots,
-               cudaStream_t stream);
+               cudaStream_t stream, const MmaScratch* scratch = nullptr);
+
+// Split-K scratch a call with these sizes needs: partial bytes and counters.
+void mma_split_needs(DeviceState* ds, int64_t N, int64_t K, int64_t M, size_t* part_bytes,
+                     int64_t* counters);
+
+// Whether the tensor-core path takes this shape at all (M >= 32, N >= 128,
+// K % 128 == 0), ignoring the AXQ8_MMA_MIN_M threshold.
+inline bool mma_shape_ok(int64_t N, int64_t K, int64_t M) {
+    return M >= 32 && M <= (1 << 24) && N >= 128 && N <= (1 << 24) && K >= 128 && K % 128 == 0 &&
+           K <= (1 << 20);
+}
 
 // Mp for a given M (row pitch of dxT).
 inline int64_t mma_scale_pitch(int64_t M) { return (M + 3) / 4 * 4; }

@@ -2,7 +2,7 @@
 """Benchmark of the B200 Q8_0 hot path; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl axion|reference]
-                    [--workload decode|gemv|prefill]
+                    [--workload decode|gemv|prefill|llama3]
 
 Workloads
   decode (default) TinyLlama-1.1B-architecture decode: 22
@@ -23,6 +23,13 @@ Workloads
          weight rotates over enough copies (> 4 x L2) that every step streams
          its weight from HBM.  Metric: algorithmic bytes / s (W 34/32 B per
          weight + x + y = 12,285,952 B per step).
+  llama3 Llama-3-8B-architecture batched decode: 32
+         layers, hidden 4096, FFN 14336, 32/8 heads of 128, vocab 128256, RoPE
+         theta 5e5 (not given by the config; Llama-3's), batch 64, random
+         2048-token prompts, then K (default 128) greedy steps; tensor parallel
+         over the N GPUs of the run (strong scaling).  Every linear runs on the
+         tcgen05 kind::i8 product at M = 64.  Metric: decode tokens/s of the
+         whole job; the reference arm is extrapolated from one linear.
   prefill Q8_0 prefill GEMM sweep: Llama-2-7B linear
          shapes [4096x4096], [11008x4096], [4096x11008], [32000x4096] x M in
          {256, 1024, 2048, 4096} on the tcgen05 kind::i8 path.  One step = one
@@ -537,6 +544,131 @@ def decode_reference(args, steps: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Llama-3-8B-architecture batched decode, tensor parallel
+# ---------------------------------------------------------------------------
+
+L3 = dict(n_layers=32, hidden=4096, ffn=14336, n_heads=32, n_kv_heads=8, head_dim=128,
+          vocab=128256, rope_theta=500000.0, rms_eps=1e-5)
+L3_BATCH, L3_PROMPT, L3_NEW, L3_SEED = 64, 2048, 128, 0x8B
+L3_METRIC = "Llama-3-8B-arch Q8_0 batched decode tokens/s (batch 64, 2048-token prompts, greedy)"
+L3_CONFIG = {"workload": "llama3_8b_arch_decode_b64_tp", "layers": 32, "hidden": 4096,
+             "ffn": 14336, "heads": "32q/8kv x 128", "vocab": 128256, "rope_theta": 500000.0,
+             "batch": L3_BATCH, "prompt": L3_PROMPT, "new_tokens": L3_NEW,
+             "kv": "paged fp16, block 16", "act": "q8 (A8W8, tcgen05 kind::i8 for M = 64)"}
+
+
+def run_llama3_axion(args, d: Dist) -> dict:
+    """One step = one greedy decode position of all 64 sequences; the job is
+    tensor parallel over the N ranks (every rank holds 1/N of each layer's
+    heads, FFN rows and LM-head vocabulary), so the whole job decodes 64
+    tokens per step (strong scaling).  The 2048-token prompts are processed
+    by the same step inside the timed call (excluded from `value`, included
+    in `e2e`)."""
+    import numpy as np
+    import torch
+    from axion_b200 import ops
+    from axion_b200.decoder import Decoder, DecoderConfig
+    dev = torch.device("cuda", d.local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    K_new, P = args.steps, args.prompt or L3_PROMPT
+    cfg = DecoderConfig(**L3, max_batch=L3_BATCH, max_ctx=P + max(K_new, args.warmup),
+                        act_mode="q8", tp_size=d.world, tp_rank=d.rank)
+    dec = Decoder(cfg)
+    dec.init_random(L3_SEED, 0.02)
+    dec.tp_connect()
+    prompts = np.random.default_rng(99).integers(0, L3["vocab"], (L3_BATCH, P)).astype(np.int32)
+    sp = stream.cuda_stream
+    dec.generate(prompts[:, :8], args.warmup, stream=sp)      # graph build + W steps
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device_uuid(dev), period_ms=50).start()
+    time.sleep(0.15)
+    d.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    toks, _, decode_ms = dec.generate(prompts, K_new, stream=sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    d.barrier()
+    clk = clocks.stop()
+    ms_max = d.max(decode_ms)
+    e2e_ms = d.max(e0.elapsed_time(e1))
+    n_tok = L3_BATCH * K_new
+    value = n_tok / (ms_max / 1e3)
+    e2e_val = n_tok / (e2e_ms / 1e3)
+    # roofline per rank: its weight slice + its KV heads read per step
+    wbytes = dec.weight_bytes_per_step
+    kv_l = L3["n_kv_heads"] // d.world
+    mean_ctx = P + (K_new - 1) / 2
+    kv_bytes = L3["n_layers"] * 2 * mean_ctx * kv_l * L3["head_dim"] * 2 * L3_BATCH
+    step_ms = ms_max / K_new
+    achieved = (wbytes + kv_bytes) / (step_ms / 1e3) / 1e9
+    peaks, peak_kind = measured_peaks()
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": None, "kernel": "decode step per rank (q8_mma_kernel dominant)",
+                "step_us": round(step_ms * 1e3, 1),
+                "algorithmic_bytes_per_step_per_rank": int(wbytes + kv_bytes),
+                "peak_source": peak_kind}
+    status = ops.status()
+    dev_bytes = dec.device_bytes
+    kernels = dec.step_kernels(L3_BATCH)
+    dec.close()
+    return {
+        "metric": L3_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": d.world,
+        "steps": K_new, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32 -> fp32 (A8W8), fp16 KV",
+        "data": "synthetic (device-generated Q8_0 weights N(0,0.02), norms 1.0; "
+                "random prompt token ids)",
+        "config": dict(L3_CONFIG, prompt=P, parallelism=f"tp{d.world} (NCCL all-reduce after "
+                       "O and down, argmax max all-reduce)", device_bytes_per_rank=dev_bytes),
+        "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": round(L3_BATCH * P * 4 / K_new, 1),
+                "d2h_bytes_per_step": L3_BATCH * 4,
+                "path": "axdec_generate (C ABI), prompt positions included"},
+        "roofline": roofline,
+        "gpu_launches": kernels * K_new,
+        "kernels_per_step": kernels,
+        "clocks": clk,
+        "device_status": status,
+        "first_tokens": [int(t) for t in toks[0][:8]],
+    }
+
+
+def llama3_reference(args, rows: int) -> dict:
+    """The reference cannot batch decode (rope_apply_row_at takes one row,
+    mha.cpp:208-211), so its rate is extrapolated: load_tensor +
+    linear_from_gguf on one [4096 x 4096] Q8_0 weight at M = `rows`, host
+    cores, gives a multiply-add rate; one batch-64 step needs 64 x (32 layers'
+    218 M + 525 M LM-head weights) multiply-adds."""
+    import numpy as np
+    from axion_b200.gguf import Q8_0, GGUFWriter
+    from oracle.oracle import Oracle, RefLib
+    o, r = Oracle(), RefLib()
+    tmp = Path(tempfile.mkdtemp()) / "l3.gguf"
+    gw = GGUFWriter()
+    gw.add_tensor("blk.0.attn_q.weight", o.synth_q8_0(L3_SEED, 4096, 4096), (4096, 4096), Q8_0)
+    gw.write(tmp)
+    x = np.random.default_rng(0).normal(0, 1, (rows, 4096)).astype(np.float32)
+    r.time_linear(tmp, "blk.0.attn_q.weight", x[:1], 4096, 1)
+    sec, _ = r.time_linear(tmp, "blk.0.attn_q.weight", x, 4096, 1)
+    tmp.unlink()
+    mac_rate = rows * 4096 * 4096 / sec
+    layer = 4096 * 4096 * 2 + 2 * 1024 * 4096 + 3 * 14336 * 4096
+    step_macs = L3_BATCH * (32 * layer + L3["vocab"] * 4096)
+    step_s = step_macs / mac_rate
+    return {"value": round(L3_BATCH / step_s, 5), "unit": "tokens/s", "cores": host_cores(),
+            "kind": "reference",
+            "sample": f"extrapolated: load_tensor + linear_from_gguf [4096x4096] Q8_0 at M={rows} "
+                      f"({sec:.2f} s, OpenMP threads={host_cores()}) scaled to one batch-64 "
+                      f"Llama-3-8B step ({step_macs / 1e12:.2f} T multiply-adds)",
+            "seconds": round(step_s, 3), "steps": 1}
+
+
+# ---------------------------------------------------------------------------
 # Prefill GEMM sweep (BASELINE config 3): Llama-2-7B linear shapes on the
 # tensor-core path
 # ---------------------------------------------------------------------------
@@ -712,6 +844,7 @@ WORKLOADS = {
              {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K, "M": 1},
              200000, 300),
     "prefill": (run_prefill_axion, prefill_reference, PREFILL_METRIC, PREFILL_CONFIG, 16, 64),
+    "llama3": (run_llama3_axion, llama3_reference, L3_METRIC, L3_CONFIG, L3_NEW, 16),
 }
 
 
@@ -722,6 +855,8 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["axion", "reference"], default="axion")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--prompt", type=int, default=None,
+                    help="llama3 workload: prompt length (default 2048)")
     ap.add_argument("--cpu-sample", type=int, default=None,
                     help="size of the reference sample timed for cpu_baseline")
     args = ap.parse_args()

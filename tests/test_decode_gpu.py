@@ -212,3 +212,31 @@ def test_tinyllama_full_workload_runs(cuda):
     assert ms_a > 0 and ms_b > 0
     assert ops.status() == 0
     d.close()
+
+
+def test_wide_batch_tensor_core_path_matches_single_sequences(cuda):
+    """32 sequences take the wide step (every linear on the tcgen05 product,
+    RoPE/KV and argmax as kernels of their own); each sequence agrees with a
+    single-sequence run of the fused GEMV step (A8 tolerances)."""
+    from axion_b200 import ops
+    from axion_b200.decoder import Decoder
+    prompts = np.random.default_rng(12).integers(0, 32000, (32, 5)).astype(np.int32)
+    d = Decoder(_tinyllama_cfg(max_batch=32, max_ctx=64))
+    d.init_random(0xA710, std=0.02)
+    toks, lg, _ = d.generate(prompts, 3, logits=True)
+    wide_kernels = d.step_kernels(32)
+    d.close()
+    assert ops.status() == 0
+    # embed; per layer rmsnorm, qkv, rope/kv, attention, o, rmsnorm, gate|up,
+    # silu, down; final rmsnorm, lm_head, argmax, advance (+ quantization-free products)
+    assert wide_kernels == 1 + 9 * 22 + 4
+    # the single-sequence step teacher-forced with the wide run's tokens (a
+    # near-tie greedy choice would otherwise fork the continuations)
+    d1 = Decoder(_tinyllama_cfg(max_batch=1, max_ctx=64))
+    d1.init_random(0xA710, std=0.02)
+    for b in (0, 17, 31):
+        seq = np.concatenate([prompts[b], toks[b][:-1]])[None]
+        l1 = d1.forced(seq, prompts.shape[1])
+        assert _rel(lg[:, b, :], l1[:, 0, :]) <= A8_TOL
+        assert _top1_consistent(lg[:, b, :], l1[:, 0, :], A8_TOL)
+    d1.close()
