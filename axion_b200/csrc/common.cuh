@@ -112,6 +112,12 @@ __device__ inline void cp_async16(void* smem_dst, const void* gmem_src) {
                  : "memory");
 }
 __device__ inline void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+__device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ inline void cp_async_wait_group() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
 
 // ---- programmatic dependent launch ----------------------------------------
 // wait: block until the preceding grid in the stream has completed and its

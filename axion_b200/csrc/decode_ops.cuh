@@ -113,7 +113,7 @@ __device__ __forceinline__ float2 kv_pair(const float* p) {
 // the split's page ids.
 template <typename KV, int HD>
 inline size_t attn_smem_bytes(int G, int cp, int bps) {
-    return (size_t)2 * cp * 16 * HD * sizeof(KV) + (size_t)G * HD * sizeof(float) +
+    return (size_t)4 * cp * 16 * HD * sizeof(KV) + (size_t)G * HD * sizeof(float) +
            ((size_t)bps * sizeof(int) + 15) / 16 * 16;
 }
 
@@ -131,9 +131,9 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
     static_assert(HD % 32 == 0 && (DL == 1 || DL % 2 == 0), "head dim");
     extern __shared__ __align__(16) uint8_t attn_sm[];
     const int G = blockDim.x >> 5;
-    KV* ks = reinterpret_cast<KV*>(attn_sm);              // [cp][B][HD]
-    KV* vs = ks + (size_t)cp * B * HD;                     // [cp][B][HD]
-    float* qs = reinterpret_cast<float*>(vs + (size_t)cp * B * HD);   // [G][HD]
+    KV* ks = reinterpret_cast<KV*>(attn_sm);              // [2][cp][B][HD] (double buffer)
+    KV* vs = ks + (size_t)2 * cp * B * HD;                 // [2][cp][B][HD]
+    float* qs = reinterpret_cast<float*>(vs + (size_t)2 * cp * B * HD);   // [G][HD]
     int* pg = reinterpret_cast<int*>(qs + G * HD);         // [bps] page ids
     const int kvh = blockIdx.x, m = blockIdx.y, s = blockIdx.z, nsplit = gridDim.z;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -158,22 +158,40 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
     for (int i = 0; i < DL; i++) acc[i] = 0.0f;
     const int t = lane & (B - 1), hf = lane >> 4;
     constexpr int per_page = B * HD / V16;
-    for (int c0 = b0; c0 < b1; c0 += cp) {
-        const int np = min(cp, b1 - c0);
-        __syncthreads();   // previous chunk consumed; pg visible
+    // chunks of cp pages, double buffered: the copy of chunk ci + 1 is in
+    // flight while chunk ci is scored
+    const int nch = b1 > b0 ? (b1 - b0 + cp - 1) / cp : 0;
+    auto issue = [&](int ci) {
+        const int c0 = b0 + ci * cp, np = min(cp, b1 - c0);
+        KV* kb = ks + (size_t)(ci & 1) * cp * B * HD;
+        KV* vb = vs + (size_t)(ci & 1) * cp * B * HD;
         for (int i = threadIdx.x; i < np * per_page; i += blockDim.x) {
             const int p = i / per_page, j = i - p * per_page;
             const int64_t off = ((int64_t)pg[c0 - b0 + p] * n_kv + kvh) * B * HD + j * V16;
-            cp_async16(ks + p * B * HD + j * V16, kc + off);
-            cp_async16(vs + p * B * HD + j * V16, vc + off);
+            cp_async16(kb + p * B * HD + j * V16, kc + off);
+            cp_async16(vb + p * B * HD + j * V16, vc + off);
         }
-        cp_async_wait_all();
+    };
+    __syncthreads();   // pg visible
+    if (nch > 0) issue(0);
+    cp_async_commit();   // group 0 also holds the query copies
+    for (int ci = 0; ci < nch; ci++) {
+        if (ci + 1 < nch) {
+            issue(ci + 1);
+            cp_async_commit();
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
+        }
         __syncthreads();
+        const int c0 = b0 + ci * cp, np = min(cp, b1 - c0);
+        const KV* kbuf = ks + (size_t)(ci & 1) * cp * B * HD;
+        const KV* vbuf = vs + (size_t)(ci & 1) * cp * B * HD;
         for (int p = 0; p < np; p++) {
             const int blk = c0 + p;
             // score of token t, half hf of the dims, then combine the halves
             const float* q = qs + warp * HD + hf * (HD / 2);
-            const KV* k = ks + ((size_t)p * B + t) * HD + hf * (HD / 2);
+            const KV* k = kbuf + ((size_t)p * B + t) * HD + hf * (HD / 2);
             float dot = 0.0f;
 #pragma unroll 8
             for (int d2 = 0; d2 < HD / 4; d2++) {
@@ -198,7 +216,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
             lrun = fmaf(lrun, corr, ps);
 #pragma unroll
             for (int i = 0; i < DL; i++) acc[i] *= corr;
-            const KV* v = vs + (size_t)p * B * HD + lane * DL;
+            const KV* v = vbuf + (size_t)p * B * HD + lane * DL;
 #pragma unroll 4
             for (int tt = 0; tt < B; tt++) {
                 const float pv = __shfl_sync(0xffffffffu, pt, tt);
@@ -215,10 +233,9 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
             }
             mrun = mnew;
         }
+        __syncthreads();   // buffer ci & 1 is free for chunk ci + 2
     }
-    if (b0 >= b1) {   // empty split: qs copies still in flight
-        cp_async_wait_all();
-    }
+    if (nch == 0) cp_async_wait_all();   // empty split: the query copies
     float* o = part + (((int64_t)m * n_heads + h) * nsplit + s) * (HD + 2);
 #pragma unroll
     for (int i = 0; i < DL; i++) o[lane * DL + i] = acc[i];

@@ -281,8 +281,8 @@ template <typename KV, int HD>
 int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s, int dxt) {
     const axdec_config_t& c = m->c;
     const int G = c.n_heads / c.n_kv_heads;
-    // pages staged at once: up to 32 KB of K and V
-    const int cp = std::max(1, std::min(m->bps, (int)(32768 / (2 * 16 * HD * sizeof(KV)))));
+    // pages per chunk: two chunks of K and V in at most 32 KB
+    const int cp = std::max(1, std::min(m->bps, (int)(32768 / (4 * 16 * HD * sizeof(KV)))));
     const size_t smem = attn_smem_bytes<KV, HD>(G, cp, m->bps);
     if (smem > 48 * 1024)
         return fail(AXQ8_ERR_UNSUPPORTED, "attention: %zu B of shared memory", smem);
@@ -663,10 +663,10 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->rs_q = q8r_row_stride(m->Nq);
     m->rs_f = q8r_row_stride(c.ffn);
     m->max_blocks = (c.max_ctx + c.kv_block - 1) / c.kv_block;
-    // split the context so that attention fills about one wave of CTAs at full
+    // split the context so that attention gives about four CTAs per SM at full
     // length, with at least 2 pages per split and at most 32 splits (the
     // merge gives one lane to each split)
-    const int target = (ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
+    const int target = (4 * ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
                        (c.n_kv_heads * c.max_batch);
     m->nsplit = std::max(1, std::min(std::min(target, (m->max_blocks + 1) / 2), 32));
     m->bps = (m->max_blocks + m->nsplit - 1) / m->nsplit;

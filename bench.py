@@ -96,6 +96,12 @@ def ncu_traffic(workload: str):
         return None
 
 
+def use_all_host_cores() -> None:
+    """The reference's OpenMP loops use every host core (torchrun sets
+    OMP_NUM_THREADS=1 for its workers); called before its library loads."""
+    os.environ["OMP_NUM_THREADS"] = str(host_cores())
+
+
 def host_cores() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -868,6 +874,7 @@ def main() -> int:
     if args.impl == "reference":
         if d.rank != 0:
             return 0
+        use_all_host_cores()
         sample = args.cpu_sample or sample_default
         cb = run_ref(args, sample)
         steps = cb.get("steps", sample)
@@ -890,6 +897,7 @@ def main() -> int:
     res = run_axion(args, d)
     if d.rank == 0:
         try:
+            use_all_host_cores()
             cb = run_ref(args, args.cpu_sample or sample_default)
             res["cpu_baseline"] = {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")}
         except Exception as e:  # the reference library did not travel / build

@@ -9,7 +9,8 @@ all-reduces.  Skipped with fewer GPUs than ranks.
   are equal.
 * A8 + fp16 KV (decode default): a last-bit difference in the hidden state
   can move one activation across a quantization boundary, so the tolerance
-  and token check are those of the single-GPU A8 tests.
+  and token check are those of the single-GPU A8 tests, and the single-GPU
+  logits are teacher-forced with the tensor-parallel run's tokens.
 * TinyLlama architecture at full size with device-generated weights: every
   rank generates exactly its slice of the single-GPU tensors.
 """
@@ -92,12 +93,14 @@ def test_tp_q8_matches_single_gpu(cuda, tmp_path):
     import _tp_worker
     from axion_b200.decoder import Decoder
     prompt = golden("tiny_llama_ref.npz")["prompt"].tolist()
-    ref = Decoder.from_gguf(golden("tiny_llama.gguf"), act_mode="q8", kv_fp32=False, max_ctx=32)
-    rt, rl, _ = ref.generate(prompt, 12, logits=True)
-    ref.close()
     _run(_tp_worker.tiny_gguf, 2, str(tmp_path), str(golden("tiny_llama.gguf")), "q8", False,
          prompt, 12)
     toks, lg = _gather(tmp_path, 2)
+    # single GPU, teacher-forced with the tensor-parallel run's tokens (a
+    # near-tie greedy choice would otherwise fork the continuations)
+    ref = Decoder.from_gguf(golden("tiny_llama.gguf"), act_mode="q8", kv_fp32=False, max_ctx=32)
+    rl = ref.forced(np.asarray(prompt + toks[0][:-1].tolist(), np.int32)[None], len(prompt))
+    ref.close()
     assert _rel(lg[:1, 0, :], rl[:1, 0, :]) <= 1e-3
     assert _rel(lg[:, 0, :], rl[:, 0, :]) <= A8_TOL
     assert _top1_consistent(lg[:, 0, :], rl[:, 0, :], A8_TOL)
@@ -113,12 +116,13 @@ def test_tp_tinyllama_architecture_batch(cuda, tmp_path, world):
     kw = dict(n_layers=22, hidden=2048, ffn=5632, n_heads=32, n_kv_heads=4, head_dim=64,
               vocab=32000, rope_theta=10000.0, rms_eps=1e-5, max_batch=3, max_ctx=64)
     prompts = np.random.default_rng(4).integers(0, 32000, (3, 6)).astype(np.int32)
-    ref = Decoder(DecoderConfig(**kw))
-    ref.init_random(0xA710, std=0.02)
-    rt, rl, _ = ref.generate(prompts, 4, logits=True)
-    ref.close()
     _run(_tp_worker.synthetic, world, str(tmp_path), kw, 0xA710, prompts.tolist(), 4)
     toks, lg = _gather(tmp_path, world)
+    # single GPU, teacher-forced with the tensor-parallel run's tokens
+    ref = Decoder(DecoderConfig(**kw))
+    ref.init_random(0xA710, std=0.02)
+    rl = ref.forced(np.concatenate([prompts, toks[:, :-1]], axis=1), prompts.shape[1])
+    ref.close()
     err = _rel(lg.reshape(4, -1), rl.reshape(4, -1))
     print(f"tp{world} tinyllama-arch A8 logits rel err vs 1 GPU: {err:.2e}")
     # 22 layers x 6 prompt positions of A8 re-quantization already separate
