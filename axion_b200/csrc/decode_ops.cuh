@@ -89,6 +89,58 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     }
 }
 
+// The split merge of one query head (one warp): out = sum_s acc_s e^(m_s - M)
+// / sum_s l_s e^(m_s - M) over the nsplit partials of (sequence m, head h),
+// then (Q8) the head's A8 quantization.  One lane per split (nsplit <= 32):
+// every partial is loaded at once.
+template <int HD, bool Q8>
+__device__ __forceinline__ void attn_merge_head(const float* __restrict__ part, int m, int n_heads,
+                                                int h, int nsplit, float* __restrict__ out,
+                                                int8_t* __restrict__ xq, float* __restrict__ dx,
+                                                int dxt, int lane) {
+    constexpr int DL = HD / 32;
+    const float* ph = part + ((int64_t)m * n_heads + h) * nsplit * (HD + 2);
+    const float ms = lane < nsplit ? __ldcg(ph + lane * (HD + 2) + HD) : -CUDART_INF_F;
+    const float ls = lane < nsplit ? __ldcg(ph + lane * (HD + 2) + HD + 1) : 0.0f;
+    float mx = ms;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    const float f = ms == -CUDART_INF_F ? 0.0f : expf(ms - mx);   // empty splits weigh 0
+    const float l = warp_sum(ls * f);
+    float sum[DL];
+#pragma unroll
+    for (int i = 0; i < DL; i++) sum[i] = 0.0f;
+#pragma unroll 4
+    for (int t2 = 0; t2 < nsplit; t2++) {
+        const float ft = __shfl_sync(0xffffffffu, f, t2);
+#pragma unroll
+        for (int i = 0; i < DL; i++) sum[i] = fmaf(__ldcg(ph + t2 * (HD + 2) + lane * DL + i), ft, sum[i]);
+    }
+    const int64_t base = (int64_t)m * n_heads * HD + (int64_t)h * HD + lane * DL;
+    float v[DL];
+#pragma unroll
+    for (int i = 0; i < DL; i++) v[i] = __fdiv_rn(sum[i], l);
+    if (!Q8) {
+#pragma unroll
+        for (int i = 0; i < DL; i++) out[base + i] = v[i];
+        return;
+    }
+    // 32-dim quantization block = 32/DL consecutive lanes
+    float am = 0.0f;
+#pragma unroll
+    for (int i = 0; i < DL; i++) am = fmaxf(am, fabsf(v[i]));
+#pragma unroll
+    for (int off = 1; off < 32 / DL; off <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
+    const float id = am == 0.0f ? 0.0f : __fdiv_rn(127.0f, am);
+#pragma unroll
+    for (int i = 0; i < DL; i++) xq[base + i] = (int8_t)q8_round(__fmul_rn(v[i], id));
+    if ((lane % (32 / DL)) == 0) {
+        const int64_t col = (int64_t)h * HD + lane * DL;   // position in the row of n_heads*HD
+        dx[dxt ? (col / QK) * dxt + m : base / QK] = __fdiv_rn(am, 127.0f);
+    }
+}
+
+
 // ---- attention: split-K flash decode ----------------------------------------------
 // Grid (n_kv, M, nsplit); G warps per CTA, warp g serving query head
 // kvh*G + g (GQA: query head h reads kv head h / G, mha.cpp:253-254).  Split
@@ -257,46 +309,282 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
     __syncthreads();
     if (!last) return;
     __threadfence();
-    // one lane per split (nsplit <= 32): every partial is loaded at once
-    const float* ph = part + ((int64_t)m * n_heads + h) * nsplit * (HD + 2);
-    const float ms = lane < nsplit ? __ldcg(ph + lane * (HD + 2) + HD) : -CUDART_INF_F;
-    const float ls = lane < nsplit ? __ldcg(ph + lane * (HD + 2) + HD + 1) : 0.0f;
-    float mx = ms;
+    attn_merge_head<HD, Q8>(part, m, n_heads, h, nsplit, out, xq, dx, dxt, lane);
+}
+
+// ---- attention on the tensor cores (fp16 KV pages, head dim 64 / 128) ---------------
+// Grid (n_kv, M, nsplit) as above; kAttnTcWarps warps per CTA, each taking
+// whole pages of the split in turn (page b0 + w, b0 + w + W, ...) for all G
+// query heads of the KV head.  Per page (16 tokens) and warp:
+//   S [16 heads (G used) x 16 tokens] = Q K^T    mma.sync m16n8k16, fp32 accumulate
+//   online softmax over the page's tokens per head (scale after the dot, as
+//   the reference does; expf)
+//   O [16 x hd] += P V                            mma.sync m16n8k16
+// Q and P are fp32 values split into an fp16 high part and an fp16 residual,
+// each multiplied separately (products with the fp16 K / V are exact in fp32),
+// so the scores and the output keep fp32 accuracy.  K and V pages are copied
+// per warp with cp.async, double buffered, into rows XOR-swizzled by 16-byte
+// chunk so that ldmatrix reads are conflict-free.  The warps' states merge in
+// shared memory into the split partial of the scalar kernel above, and the
+// last split CTA merges the splits with attn_merge_head.
+constexpr int kAttnTcWarps = 4;
+
+// Shared memory: the warps' double-buffered K/V pages, reused afterwards for
+// the warps' merge ([W][16 x HD + 32] fp32), then the split's page ids.
+template <int HD>
+struct AttnTcSmem {
+    static constexpr size_t STAGE = (size_t)kAttnTcWarps * 2 /*buffers*/ * 2 /*K,V*/ * 16 * HD * 2;
+    static constexpr size_t MERGE = (size_t)kAttnTcWarps * (16 * HD + 32) * 4;
+    static constexpr size_t PG = STAGE > MERGE ? STAGE : MERGE;   // offset of the page ids
+};
+template <int HD>
+inline size_t attn_tc_smem_bytes(int bps) {
+    return AttnTcSmem<HD>::PG + ((size_t)bps * sizeof(int) + 15) / 16 * 16;
+}
+
+__device__ __forceinline__ void mma_f16_16816(float* c, const uint32_t* a, uint32_t b0, uint32_t b1) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, "
+        "{%8, %9}, {%0, %1, %2, %3};"
+        : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4(uint32_t* r, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t* r, uint32_t addr) {
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(addr));
+}
+// fp16 pair (lo element first) of x and y, and of their fp16 residuals.
+__device__ __forceinline__ void split_pair(float x, float y, uint32_t& hi, uint32_t& lo) {
+    const __half xh = __float2half_rn(x), yh = __float2half_rn(y);
+    const __half xl = __float2half_rn(x - __half2float(xh)), yl = __float2half_rn(y - __half2float(yh));
+    hi = (uint32_t)__half_as_ushort(xh) | ((uint32_t)__half_as_ushort(yh) << 16);
+    lo = (uint32_t)__half_as_ushort(xl) | ((uint32_t)__half_as_ushort(yl) << 16);
+}
+
+template <int HD, bool Q8>
+__global__ void __launch_bounds__(kAttnTcWarps * 32)
+    attn_tc_kernel(const float* __restrict__ qkv, int ldq, const int* __restrict__ pos,
+                   const __half* __restrict__ kc, const __half* __restrict__ vc,
+                   const int* __restrict__ block_table, int max_blocks, int n_heads, int n_kv,
+                   int G, int bps, float scale, float* __restrict__ part, int* __restrict__ counters,
+                   float* __restrict__ out, int8_t* __restrict__ xq, float* __restrict__ dx, int dxt) {
+    constexpr int B = 16;
+    constexpr int W = kAttnTcWarps;
+    constexpr int KS = HD / 16;              // k-steps of the score product
+    constexpr int NT = HD / 8;               // n-tiles (8 dims) of the output
+    constexpr int CH = HD / 8;               // 16-byte chunks per row
+    constexpr int PAGE = B * HD;             // halves per K (or V) page
+    extern __shared__ __align__(16) uint8_t tc_sm[];
+    __half* stage = reinterpret_cast<__half*>(tc_sm);   // [W][2 buf][K,V][B][HD]
+    int* pg = reinterpret_cast<int*>(tc_sm + AttnTcSmem<HD>::PG);
+    const int kvh = blockIdx.x, m = blockIdx.y, s = blockIdx.z, nsplit = gridDim.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int b0 = s * bps;
+    for (int i = threadIdx.x; i < bps; i += blockDim.x)
+        pg[i] = b0 + i < max_blocks ? block_table[m * max_blocks + b0 + i] : 0;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int ctx = min(pos[m] + 1, max_blocks * B);
+    const int nblk = (ctx + B - 1) / B;
+    const int b1 = min(nblk, b0 + bps);
+    __syncthreads();   // pg visible
+    // Q fragments (rows = heads kvh*G + row, rows >= G zero), fp16 high and residual
+    uint32_t qh[KS][4], ql[KS][4];
+    {
+        const float* q0 = qkv + (int64_t)m * ldq + (int64_t)(kvh * G) * HD;
 #pragma unroll
-    for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    const float f = ms == -CUDART_INF_F ? 0.0f : expf(ms - mx);   // empty splits weigh 0
-    const float l = warp_sum(ls * f);
-    float sum[DL];
+        for (int k = 0; k < KS; k++) {
 #pragma unroll
-    for (int i = 0; i < DL; i++) sum[i] = 0.0f;
-#pragma unroll 4
-    for (int t2 = 0; t2 < nsplit; t2++) {
-        const float ft = __shfl_sync(0xffffffffu, f, t2);
-#pragma unroll
-        for (int i = 0; i < DL; i++) sum[i] = fmaf(__ldcg(ph + t2 * (HD + 2) + lane * DL + i), ft, sum[i]);
+            for (int r = 0; r < 4; r++) {
+                const int row = g + ((r & 1) ? 8 : 0);
+                const int col = k * 16 + 2 * t + ((r & 2) ? 8 : 0);
+                float x = 0.0f, y = 0.0f;
+                if (row < G) {
+                    const float2 v = *reinterpret_cast<const float2*>(q0 + (int64_t)row * HD + col);
+                    x = v.x;
+                    y = v.y;
+                }
+                split_pair(x, y, qh[k][r], ql[k][r]);
+            }
+        }
     }
-    const int64_t base = (int64_t)m * n_heads * HD + (int64_t)h * HD + lane * DL;
-    float v[DL];
+    float o[NT][4];
 #pragma unroll
-    for (int i = 0; i < DL; i++) v[i] = __fdiv_rn(sum[i], l);
-    if (!Q8) {
+    for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float mrun[2] = {-CUDART_INF_F, -CUDART_INF_F}, lrun[2] = {0.0f, 0.0f};
+    __half* wst = stage + (size_t)warp * 2 * 2 * PAGE;
+    const uint32_t wst_s = smem_u32(wst);
+    // this warp's pages: b0 + warp, b0 + warp + W, ...
+    const int npw = b1 > b0 + warp ? (b1 - b0 - warp + W - 1) / W : 0;
+    auto issue = [&](int i) {            // page number i of this warp -> buffer i & 1
+        const int blk = b0 + warp + i * W;
+        const int64_t off = ((int64_t)pg[blk - b0] * n_kv + kvh) * PAGE;
+        __half* kb = wst + (size_t)(i & 1) * 2 * PAGE;
+        __half* vb = kb + PAGE;
 #pragma unroll
-        for (int i = 0; i < DL; i++) out[base + i] = v[i];
-        return;
+        for (int c = lane; c < B * CH; c += 32) {
+            const int r = c / CH, ch = c % CH;
+            const int sw = r * HD + ((ch ^ (r & 7)) * 8);
+            cp_async16(kb + sw, kc + off + r * HD + ch * 8);
+            cp_async16(vb + sw, vc + off + r * HD + ch * 8);
+        }
+    };
+    if (npw > 0) issue(0);
+    cp_async_commit();
+    for (int i = 0; i < npw; i++) {
+        if (i + 1 < npw) {
+            issue(i + 1);
+            cp_async_commit();
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
+        }
+        __syncwarp();
+        const int blk = b0 + warp + i * W;
+        const uint32_t kb = wst_s + (uint32_t)((i & 1) * 2 * PAGE * 2);
+        const uint32_t vb = kb + PAGE * 2;
+        // S = Q K^T: n-tile 0 = tokens 0-7, n-tile 1 = tokens 8-15
+        float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+        {
+            const int mi = lane >> 3, rr = lane & 7;
+            const int tok = rr + ((mi >> 1) << 3);
+#pragma unroll
+            for (int k = 0; k < KS; k++) {
+                const int ch = k * 2 + (mi & 1);
+                uint32_t kf[4];
+                ldsm_x4(kf, kb + (uint32_t)((tok * HD + ((ch ^ (tok & 7)) * 8)) * 2));
+                mma_f16_16816(sc[0], qh[k], kf[0], kf[1]);
+                mma_f16_16816(sc[0], ql[k], kf[0], kf[1]);
+                mma_f16_16816(sc[1], qh[k], kf[2], kf[3]);
+                mma_f16_16816(sc[1], ql[k], kf[2], kf[3]);
+            }
+        }
+        // online softmax per head row (g: c0, c1; g + 8: c2, c3)
+        float p[2][4];
+#pragma unroll
+        for (int hr = 0; hr < 2; hr++) {
+            float mt = -CUDART_INF_F;
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int tok = blk * B + n * 8 + 2 * t + j;
+                    float& v = sc[n][2 * hr + j];
+                    v = tok < ctx ? __fmul_rn(v, scale) : -CUDART_INF_F;
+                    mt = fmaxf(mt, v);
+                }
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+            const float mnew = fmaxf(mrun[hr], mt);
+            const float corr = expf(mrun[hr] - mnew);   // 0 when mrun is -inf
+            float ps = 0.0f;
+#pragma unroll
+            for (int n = 0; n < 2; n++)
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const float v = sc[n][2 * hr + j];
+                    const float e = v == -CUDART_INF_F ? 0.0f : expf(v - mnew);
+                    p[n][2 * hr + j] = e;
+                    ps += e;
+                }
+            lrun[hr] = fmaf(lrun[hr], corr, ps);
+            mrun[hr] = mnew;
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                o[n][2 * hr] *= corr;
+                o[n][2 * hr + 1] *= corr;
+            }
+        }
+        // P fragments (A operand, rows = heads, k = tokens) from the S layout
+        uint32_t ph[4], pl[4];
+        split_pair(p[0][0], p[0][1], ph[0], pl[0]);
+        split_pair(p[0][2], p[0][3], ph[1], pl[1]);
+        split_pair(p[1][0], p[1][1], ph[2], pl[2]);
+        split_pair(p[1][2], p[1][3], ph[3], pl[3]);
+        // O += P V: pairs of 8-dim n-tiles per ldmatrix.trans
+        {
+            const int mi = lane >> 3, rr = lane & 7;
+            const int tok = rr + ((mi & 1) << 3);
+#pragma unroll
+            for (int dn = 0; dn < HD / 16; dn++) {
+                const int ch = dn * 2 + (mi >> 1);
+                uint32_t vf[4];
+                ldsm_x4_t(vf, vb + (uint32_t)((tok * HD + ((ch ^ (tok & 7)) * 8)) * 2));
+                mma_f16_16816(o[2 * dn], ph, vf[0], vf[1]);
+                mma_f16_16816(o[2 * dn], pl, vf[0], vf[1]);
+                mma_f16_16816(o[2 * dn + 1], ph, vf[2], vf[3]);
+                mma_f16_16816(o[2 * dn + 1], pl, vf[2], vf[3]);
+            }
+        }
+        __syncwarp();   // buffer i & 1 free for page i + 2
     }
-    // 32-dim quantization block = 32/DL consecutive lanes
-    float am = 0.0f;
+    if (npw == 0) cp_async_wait_all();
+    // row sums over the quad
 #pragma unroll
-    for (int i = 0; i < DL; i++) am = fmaxf(am, fabsf(v[i]));
-#pragma unroll
-    for (int off = 1; off < 32 / DL; off <<= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, off));
-    const float id = am == 0.0f ? 0.0f : __fdiv_rn(127.0f, am);
-#pragma unroll
-    for (int i = 0; i < DL; i++) xq[base + i] = (int8_t)q8_round(__fmul_rn(v[i], id));
-    if ((lane % (32 / DL)) == 0) {
-        const int64_t col = (int64_t)h * HD + lane * DL;   // position in the row of n_heads*HD
-        dx[dxt ? (col / QK) * dxt + m : base / QK] = __fdiv_rn(am, 127.0f);
+    for (int hr = 0; hr < 2; hr++) {
+        lrun[hr] += __shfl_xor_sync(0xffffffffu, lrun[hr], 1);
+        lrun[hr] += __shfl_xor_sync(0xffffffffu, lrun[hr], 2);
     }
+    // merge the warps: per warp [16 rows][HD] of O, then 16 m, 16 l
+    __syncthreads();   // every warp is done with the staging buffers
+    float* mw = reinterpret_cast<float*>(tc_sm) + (size_t)warp * (16 * HD + 32);
+#pragma unroll
+    for (int n = 0; n < NT; n++) {
+        mw[g * HD + n * 8 + 2 * t] = o[n][0];
+        mw[g * HD + n * 8 + 2 * t + 1] = o[n][1];
+        mw[(g + 8) * HD + n * 8 + 2 * t] = o[n][2];
+        mw[(g + 8) * HD + n * 8 + 2 * t + 1] = o[n][3];
+    }
+    if (t == 0) {
+        mw[16 * HD + g] = mrun[0];
+        mw[16 * HD + g + 8] = mrun[1];
+        mw[16 * HD + 16 + g] = lrun[0];
+        mw[16 * HD + 16 + g + 8] = lrun[1];
+    }
+    __syncthreads();
+    const float* m0p = reinterpret_cast<const float*>(tc_sm);
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+        const int row = idx / HD, d = idx % HD;
+        float mx = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < W; w++) mx = fmaxf(mx, m0p[(size_t)w * (16 * HD + 32) + 16 * HD + row]);
+        float acc = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; w++) {
+            const float* base = m0p + (size_t)w * (16 * HD + 32);
+            const float mwv = base[16 * HD + row];
+            const float f = mwv == -CUDART_INF_F ? 0.0f : expf(mwv - mx);
+            acc = fmaf(base[row * HD + d], f, acc);
+            l = fmaf(base[16 * HD + 16 + row], f, l);
+        }
+        const int h = kvh * G + row;
+        float* op = part + (((int64_t)m * n_heads + h) * nsplit + s) * (HD + 2);
+        op[d] = acc;
+        if (d == 0) {
+            op[HD] = mx;
+            op[HD + 1] = l;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) {
+        int* c = counters + m * n_kv + kvh;
+        last = atomicAdd(c, 1) == nsplit - 1;
+        if (last) *c = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int hh = warp; hh < G; hh += W)
+        attn_merge_head<HD, Q8>(part, m, n_heads, kvh * G + hh, nsplit, out, xq, dx, dxt, lane);
 }
 
 // ---- RoPE + KV append over product rows (wide batches) ---------------------------

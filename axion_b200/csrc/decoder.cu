@@ -29,6 +29,7 @@
 #include <cmath>
 #include <map>
 #include <string>
+#include <type_traits>
 #include <vector>
 
 #include "axdec.h"
@@ -281,6 +282,37 @@ template <typename KV, int HD>
 int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s, int dxt) {
     const axdec_config_t& c = m->c;
     const int G = c.n_heads / c.n_kv_heads;
+    if constexpr (std::is_same<KV, __half>::value && HD >= 64) {
+      if (M >= 2) {
+        // fp16 pages, head dim 64 / 128, batches: the tensor-core kernel (one
+        // sequence with short splits keeps the scalar kernel, whose single
+        // pass has less set-up per CTA)
+        const size_t smem = attn_tc_smem_bytes<HD>(m->bps);
+        const bool q8 = c.act_mode != AXQ8_ACT_F32;
+        auto kern = q8 ? attn_tc_kernel<HD, true> : attn_tc_kernel<HD, false>;
+        static int configured[2][64] = {{0}};
+        const int dev = m->ds->device < 64 ? m->ds->device : 63;
+        constexpr int kMaxSmem = 200 * 1024;
+        if (smem > (size_t)kMaxSmem)
+            return fail(AXQ8_ERR_UNSUPPORTED, "attention: %zu B of shared memory", smem);
+        if (smem > 48 * 1024 && !configured[q8][dev]) {
+            AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               kMaxSmem),
+                          "attention smem attribute");
+            configured[q8][dev] = 1;
+        }
+        Layer& Ly = m->L[layer];
+        const float scale = 1.0f / std::sqrt((float)HD);   // mha.cpp:250
+        AXQ8_CUDA_TRY(launch_k(kern, dim3(c.n_kv_heads, M, m->nsplit), dim3(kAttnTcWarps * 32),
+                               smem, s, true, (const float*)m->qkv, m->Nqkv, (const int*)m->pos,
+                               (const __half*)Ly.kc, (const __half*)Ly.vc,
+                               (const int*)m->block_table, m->max_blocks, c.n_heads,
+                               c.n_kv_heads, G, m->bps, scale, m->part, m->attn_cnt, m->x32,
+                               m->xq, m->dx, dxt),
+                      "attention launch");
+        return AXQ8_OK;
+      }
+    }
     // pages per chunk: two chunks of K and V in at most 32 KB
     const int cp = std::max(1, std::min(m->bps, (int)(32768 / (4 * 16 * HD * sizeof(KV)))));
     const size_t smem = attn_smem_bytes<KV, HD>(G, cp, m->bps);

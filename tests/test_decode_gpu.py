@@ -240,3 +240,41 @@ def test_wide_batch_tensor_core_path_matches_single_sequences(cuda):
         assert _rel(lg[:, b, :], l1[:, 0, :]) <= A8_TOL
         assert _top1_consistent(lg[:, b, :], l1[:, 0, :], A8_TOL)
     d1.close()
+
+
+def test_tensor_core_attention_f32_vs_oracle(cuda, oracle):
+    """Head dim 64 with fp16 pages and a batch runs the mma.sync attention:
+    in A32 mode (the reference's arithmetic) two layers of the TinyLlama
+    shape over 40 prompt positions (3 pages, several warps per split; two
+    sequences, the second a different prompt) agree with the oracle holding
+    the same fp16 cache to REL_TOL."""
+    from axion_b200.decoder import Decoder
+    from oracle.model import LlamaConfig, OracleLlama
+    cfg = _tinyllama_cfg(max_ctx=64, act_mode="f32", max_batch=2)
+    cfg.n_layers = 2
+    d = Decoder(cfg)
+    seed = 0x51
+    d.init_random(seed, std=0.02)
+    rng = np.random.default_rng(8)
+    prompt = rng.integers(0, 32000, 40).tolist()
+    other = rng.integers(0, 32000, 40).tolist()
+    toks, lg, _ = d.generate(np.asarray([prompt, other], np.int32), 3, logits=True)
+    t = {}
+    shapes = {"attn_q": (2048, 2048), "attn_k": (256, 2048), "attn_v": (256, 2048),
+              "attn_output": (2048, 2048), "ffn_gate": (5632, 2048), "ffn_up": (5632, 2048),
+              "ffn_down": (2048, 5632)}
+    names = ["token_embd.weight", "output.weight"] + [
+        f"blk.{i}.{k}.weight" for i in range(2) for k in shapes]
+    for n in names:
+        N, K = (32000, 2048) if not n.startswith("blk.") else shapes[n.split(".")[2]]
+        t[n] = ("q8", oracle.synth_q8_0(seed + d.tensor_index(n), N, K, 0.02), N, K)
+    ones = np.ones(2048, np.float32)
+    t["output_norm.weight"] = ("f32", ones)
+    for i in range(2):
+        t[f"blk.{i}.attn_norm.weight"] = ("f32", ones)
+        t[f"blk.{i}.ffn_norm.weight"] = ("f32", ones)
+    om = OracleLlama(LlamaConfig(2, 2048, 32, 4, 64, 5632, 32000, 10000.0, 1e-5), t, oracle)
+    o_logits, o_toks = om.decode(prompt, 3, act="f32", kv="f16")
+    assert toks[0].tolist() == o_toks
+    assert _rel(lg[:, 0, :], o_logits) <= REL_TOL
+    d.close()
