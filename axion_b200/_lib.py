@@ -23,6 +23,7 @@ AXQ8_ACT_F32 = 1
 
 AXQ8_PATH_GEMV = 0
 AXQ8_PATH_TENSOR_CORE = 1
+AXQ8_PATH_SKINNY = 2
 
 
 class axq8_weight_t(C.Structure):
@@ -70,6 +71,7 @@ SIGNATURES: dict[str, tuple] = {
     "axq8_linear_path": (_I32, [_W, _I64, _I32]),
     "axq8_quantize_act_t": (_I32, [_P, _I64, _I64, _P, _P, _P]),
     "axq8_linear_q8act_t": (_I32, [_W, _P, _P, _I64, _P, _P, _P]),
+    "axq8_linear_q8act_s": (_I32, [_W, _P, _P, _I64, _P, _P, _P]),
     "axq8_quantize_weight_tensor": (_I32, [_P, _I64, _I64, _P, _P, _P]),
     "axq8_quantized_matmul": (_I32, [_P, _I64, _I64, _P, _P, _I64, _P, _P]),
     "axq8_synth_q8_0": (_I32, [C.c_uint64, _I64, _I64, C.c_float, C.c_float, _I32, _P, _P]),

@@ -111,6 +111,12 @@ __device__ inline void cp_async16(void* smem_dst, const void* gmem_src) {
                  "l"(gmem_src)
                  : "memory");
 }
+// 16 bytes, or zeros when `valid` is false (src-size 0: nothing is read).
+__device__ inline void cp_async16_zfill(void* smem_dst, const void* gmem_src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(smem_u32(smem_dst)),
+                 "l"(gmem_src), "r"(valid ? 16 : 0)
+                 : "memory");
+}
 __device__ inline void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Wait until at most N of this thread's committed cp.async groups are pending.

@@ -346,8 +346,10 @@ int launch_rmsnorm(axdec_model* m, int M, const float* x, const float* w, cudaSt
     return AXQ8_OK;
 }
 
-// Whether a step of M sequences runs wide: A8, M >= 32 and every linear
-// tiled by the tensor-core product.
+// Whether a step of M sequences runs wide: A8, M >= kWideMinM (the fused
+// GEMV step re-reads its weights every 4 rows beyond that), up to 64 rows on
+// the skinny product, beyond on the tcgen05 product when it tiles every linear.
+constexpr int kWideMinM = 9;
 bool wide_step(const axdec_model* m, int M) {
     // AXDEC_NARROW=1 keeps every batch on the GEMV step (comparison runs)
     static const bool narrow = [] {
@@ -357,9 +359,25 @@ bool wide_step(const axdec_model* m, int M) {
     if (narrow) return false;
     const axdec_config_t& c = m->c;
     const int64_t H = c.hidden, F = c.ffn;
-    return c.act_mode == AXQ8_ACT_Q8 && M >= 32 && mma_shape_ok(m->Nqkv, H, M) &&
-           mma_shape_ok(H, m->Nq, M) && mma_shape_ok(2 * F, H, M) && mma_shape_ok(H, F, M) &&
-           mma_shape_ok(c.vocab, H, M);
+    if (c.act_mode != AXQ8_ACT_Q8 || M < kWideMinM) return false;
+    if (M <= kMmqMaxM) return true;   // skinny product: any shape (K % 32 == 0)
+    return mma_shape_ok(m->Nqkv, H, M) && mma_shape_ok(H, m->Nq, M) &&
+           mma_shape_ok(2 * F, H, M) && mma_shape_ok(H, F, M) && mma_shape_ok(c.vocab, H, M);
+}
+
+// Widths up to which wide steps prefer the skinny product (AXDEC_SKINNY_M
+// overrides the library default of 32, up to 64, for tuning).
+int skinny_prefer_m() {
+    static const int v = [] {
+        const char* e = getenv("AXDEC_SKINNY_M");
+        const int x = e ? atoi(e) : kMmqPreferM;
+        return x >= 0 && x <= kMmqMaxM ? x : kMmqPreferM;
+    }();
+    return v;
+}
+
+bool use_skinny(int64_t N, int64_t K, int M) {
+    return M <= skinny_prefer_m() || (M <= kMmqMaxM && !mma_shape_ok(N, K, M));
 }
 
 int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
@@ -370,12 +388,13 @@ int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M
     w.K = K;
     w.row_stride = q8r_row_stride(K);
     w.device = m->ds->device;
+    if (use_skinny(N, K, M)) return mmq_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, s, &m->mma_sc);
     return mma_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, nullptr, s, &m->mma_sc);
 }
 
-// Wide batches (M >= 32, prefill-like widths of batched decode): every linear
-// on the tensor cores (tcgen05 kind::i8) from A8 activations with transposed
-// block scales, the producers (RMSNorm, SiLU*up, attention) writing that
+// Wide batches (M >= 9): every linear on the tensor cores (the skinny
+// mma.sync product up to 64 rows, tcgen05 kind::i8 beyond) from A8
+// activations with transposed block scales, the producers (RMSNorm, SiLU*up, attention) writing that
 // layout, RoPE + KV append and the greedy argmax as kernels of their own.
 template <typename KV>
 int launch_step_wide(axdec_model* m, int M, cudaStream_t s) {
@@ -743,18 +762,20 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->amax_key = (unsigned long long*)dalloc(m, sizeof(unsigned long long) * M, &rc);
     m->done = (int*)dalloc(m, sizeof(int), &rc);
     m->attn_cnt = (int*)dalloc(m, sizeof(int) * M * c.n_kv_heads, &rc);
-    if (rc == AXQ8_OK && c.act_mode == AXQ8_ACT_Q8 && M >= 32) {
+    if (rc == AXQ8_OK && c.act_mode == AXQ8_ACT_Q8 && M >= kWideMinM) {
         // split-K scratch for every width a wide step may run at
         size_t part = 0;
         int64_t cnt = 0;
         const int64_t shapes[5][2] = {{m->Nqkv, H}, {H, m->Nq}, {2 * (int64_t)F, H}, {H, F},
                                       {c.vocab, H}};
-        for (int mm = 32; mm <= M; mm++)
+        for (int mm = kWideMinM; mm <= M; mm++)
             for (auto& sh : shapes) {
-                if (!mma_shape_ok(sh[0], sh[1], mm)) continue;
-                size_t pb;
-                int64_t cn;
-                mma_split_needs(ds, sh[0], sh[1], mm, &pb, &cn);
+                size_t pb = 0;
+                int64_t cn = 0;
+                if (use_skinny(sh[0], sh[1], mm))
+                    mmq_split_needs(ds, sh[0], sh[1], mm, &pb, &cn);
+                else if (mma_shape_ok(sh[0], sh[1], mm))
+                    mma_split_needs(ds, sh[0], sh[1], mm, &pb, &cn);
                 part = std::max(part, pb);
                 cnt = std::max(cnt, cn);
             }
@@ -794,6 +815,15 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
         if (e == cudaSuccess) e = cudaMemset(m->amax_key, 0, sizeof(unsigned long long) * M);
         if (e == cudaSuccess) e = cudaMemset(m->done, 0, sizeof(int));
         if (e == cudaSuccess) e = cudaMemset(m->attn_cnt, 0, sizeof(int) * M * c.n_kv_heads);
+        // KV pages start at zero: attention multiplies the token slots past the
+        // context by a zero weight, which an uninitialized NaN pattern would
+        // turn into NaN
+        const size_t page_bytes =
+            (size_t)pages * c.n_kv_heads * c.kv_block * c.head_dim * kvsz;
+        for (int l = 0; l < c.n_layers && e == cudaSuccess; l++) {
+            e = cudaMemset(m->L[l].kc, 0, page_bytes);
+            if (e == cudaSuccess) e = cudaMemset(m->L[l].vc, 0, page_bytes);
+        }
         if (e == cudaSuccess) {
             const int ctl[4] = {1, 1, 0, 0};
             e = cudaMemcpy(m->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice);

@@ -404,8 +404,8 @@ int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int
     }
     if (act_mode != AXQ8_ACT_Q8) return fail(AXQ8_ERR_INVALID, "axq8_linear: bad act_mode %d", act_mode);
     const int64_t nb = w->K / QK;
-    if (mma_eligible(w, M)) {
-        // tensor-core path: xq [M][K] + transposed scales dxT [K/32][Mp]
+    if (skinny_eligible(w, M) || mma_eligible(w, M)) {
+        // tensor-core paths: xq [M][K] + transposed scales dxT [K/32][Mp]
         const size_t q_bytes = ((size_t)M * w->K + 255) / 256 * 256;
         const size_t d_bytes = sizeof(float) * (size_t)nb * mma_scale_pitch(M);
         uint8_t* ws = static_cast<uint8_t*>(workspace(ds, q_bytes + d_bytes));
@@ -413,6 +413,7 @@ int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int
         int8_t* xq = reinterpret_cast<int8_t*>(ws);
         float* dxT = reinterpret_cast<float*>(ws + q_bytes);
         if ((rc = mma_quantize(ds, x, M, w->K, xq, dxT, s))) return rc;
+        if (skinny_eligible(w, M)) return mmq_linear(ds, w, xq, dxT, M, nullptr, y, w->N, s);
         return mma_linear(ds, w, xq, dxT, M, nullptr, y, w->N, nullptr, s);
     }
     const size_t q_bytes = ((size_t)M * w->K + 255) / 256 * 256;

@@ -9,6 +9,7 @@
 
 #include "q8_mma.cuh"
 #include "q8_mma.h"
+#include "q8_mmq.cuh"
 
 namespace axq8 {
 namespace {
@@ -107,6 +108,11 @@ int launch_bn(DeviceState* ds, const CUtensorMap& tw, const CUtensorMap& tx, con
 }
 
 }  // namespace
+
+bool skinny_eligible(const axq8_weight_t* w, int64_t M) {
+    if (!w || M <= 8 || M > kMmqMaxM || w->K % QK || w->K > (1 << 24)) return false;
+    return M <= kMmqPreferM || !mma_eligible(w, M);
+}
 
 bool mma_eligible(const axq8_weight_t* w, int64_t M) {
     return w && M >= min_m() && M <= (1 << 24) && w->N >= kMmaBM && w->N <= (1 << 24) &&
@@ -207,6 +213,79 @@ int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const 
     return launch_bn<32, false>(ds, tw, tx, td, a, grid, stream);
 }
 
+namespace {
+struct MmqPlan {
+    int splits, per;
+    int64_t tiles;
+};
+MmqPlan mmq_plan(DeviceState* ds, int64_t N, int64_t K, int64_t M) {
+    MmqPlan p;
+    p.tiles = (N + kMmqRows - 1) / kMmqRows;
+    const int nch = (int)((K / 32 + kMmqChunkKb - 1) / kMmqChunkKb);
+    const int64_t want = 2 * (int64_t)ds->sm_count;   // two CTAs per SM
+    int splits = (int)std::max<int64_t>(1, (want + p.tiles - 1) / p.tiles);
+    splits = std::min(splits, std::max(1, nch / 2));   // >= two chunks per split
+    p.per = (nch + splits - 1) / splits;
+    p.splits = (nch + p.per - 1) / p.per;
+    return p;
+}
+template <int MT8>
+int mmq_launch(const MmqArgs& a, dim3 grid, cudaStream_t s) {
+    AXQ8_CUDA_TRY(launch_k(q8_mmq_kernel<MT8>, grid, dim3(kMmqWarps * 32), 0, s, true, a),
+                  "q8_mmq launch");
+    return AXQ8_OK;
+}
+}  // namespace
+
+void mmq_split_needs(DeviceState* ds, int64_t N, int64_t K, int64_t M, size_t* part_bytes,
+                     int64_t* counters) {
+    const MmqPlan p = mmq_plan(ds, N, K, M);
+    *part_bytes = p.splits > 1 ? sizeof(float) * (size_t)p.splits * M * N : 0;
+    *counters = p.splits > 1 ? p.tiles : 0;
+}
+
+int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
+               int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream,
+               const MmaScratch* scratch) {
+    if (!w || M < 1 || M > kMmqMaxM || w->K % QK || w->K > (1 << 24) || w->N > (1 << 30) ||
+        !xq || !dxT || !y || ldy < w->N)
+        return fail(AXQ8_ERR_INVALID, "skinny linear: unsupported arguments");
+    const MmqPlan plan = mmq_plan(ds, w->N, w->K, M);
+    if (plan.tiles > 65535 * 32) return fail(AXQ8_ERR_UNSUPPORTED, "skinny linear: N too large");
+    MmqArgs a = {};
+    a.rows = static_cast<const uint8_t*>(w->rows);
+    a.row_stride = w->row_stride;
+    a.N = (int)w->N;
+    a.K = (int)w->K;
+    a.M = (int)M;
+    a.xq = xq;
+    a.dxT = dxT;
+    a.Mp = (int)mma_scale_pitch(M);
+    a.chunks_per_split = plan.per;
+    a.residual = residual;
+    a.y = y;
+    a.ldy = (int)ldy;
+    if (plan.splits > 1) {
+        const size_t need = sizeof(float) * (size_t)plan.splits * M * w->N;
+        if (scratch) {
+            if (scratch->part_bytes < need || scratch->counter_slots < plan.tiles)
+                return fail(AXQ8_ERR_INVALID, "skinny linear: caller scratch too small");
+            a.part = scratch->part;
+            a.counters = scratch->counters;
+        } else {
+            if (plan.tiles > kCounterSlots)
+                return fail(AXQ8_ERR_UNSUPPORTED, "skinny linear: too many split tiles");
+            int rc = split_scratch(ds, need, &a.part, &a.counters);
+            if (rc) return rc;
+        }
+    }
+    const dim3 grid((unsigned)plan.tiles, (unsigned)plan.splits);
+    if (M <= 8) return mmq_launch<1>(a, grid, stream);
+    if (M <= 16) return mmq_launch<2>(a, grid, stream);
+    if (M <= 32) return mmq_launch<4>(a, grid, stream);
+    return mmq_launch<8>(a, grid, stream);
+}
+
 int mma_quantize(DeviceState* ds, const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,
                  cudaStream_t stream) {
     const int64_t nblocks = M * (K / QK);
@@ -241,7 +320,24 @@ extern "C" {
 
 int axq8_linear_path(const axq8_weight_t* w, int64_t M, int act_mode) {
     if (!w || M < 0) return fail(AXQ8_ERR_INVALID, "axq8_linear_path: bad argument");
-    return act_mode == AXQ8_ACT_Q8 && mma_eligible(w, M) ? AXQ8_PATH_TENSOR_CORE : AXQ8_PATH_GEMV;
+    if (act_mode != AXQ8_ACT_Q8) return AXQ8_PATH_GEMV;
+    if (skinny_eligible(w, M)) return AXQ8_PATH_SKINNY;
+    return mma_eligible(w, M) ? AXQ8_PATH_TENSOR_CORE : AXQ8_PATH_GEMV;
+}
+
+int axq8_linear_q8act_s(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
+                        const float* residual, float* y, void* stream) {
+    if (!w || !w->rows) return fail(AXQ8_ERR_INVALID, "axq8_linear_q8act_s: null weight");
+    if (w->row_stride != q8r_row_stride(w->K) || (reinterpret_cast<uintptr_t>(w->rows) & 15))
+        return fail(AXQ8_ERR_INVALID, "axq8_linear_q8act_s: weight not in the repacked layout");
+    if (M < 1 || M > kMmqMaxM)
+        return fail(AXQ8_ERR_UNSUPPORTED, "axq8_linear_q8act_s: needs 1 <= M <= 64 (M=%lld)",
+                    (long long)M);
+    if ((reinterpret_cast<uintptr_t>(xq) & 15) || (reinterpret_cast<uintptr_t>(dxT) & 3))
+        return fail(AXQ8_ERR_INVALID, "axq8_linear_q8act_s: misaligned xq/dxT");
+    DeviceState* ds = device_state();
+    if (!ds) return AXQ8_ERR_CUDA;
+    return mmq_linear(ds, w, xq, dxT, M, residual, y, w->N, static_cast<cudaStream_t>(stream));
 }
 
 int axq8_quantize_act_t(const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,

@@ -18,6 +18,14 @@ constexpr int kMmaMinM = 32;
 // N >= 128, K a multiple of 128.
 bool mma_eligible(const axq8_weight_t* w, int64_t M);
 
+// Widths up to which the skinny product is preferred where both apply (the
+// tcgen05 product is faster from 33 rows on large weights, measured).
+constexpr int kMmqPreferM = 32;
+
+// Whether axq8_linear takes the skinny product for w at M rows: 8 < M <= 32,
+// or 32 < M <= 64 where the tcgen05 product does not tile the shape.
+bool skinny_eligible(const axq8_weight_t* w, int64_t M);
+
 // Caller-owned split-K scratch (partials and per-tile counters, the counters
 // zero before first use); without it the library's per-device scratch is used
 // (allocated, and grown, on demand: not usable inside a graph capture).
@@ -46,6 +54,16 @@ inline bool mma_shape_ok(int64_t N, int64_t K, int64_t M) {
     return M >= 32 && M <= (1 << 24) && N >= 128 && N <= (1 << 24) && K >= 128 && K % 128 == 0 &&
            K <= (1 << 20);
 }
+
+// Skinny product for decode widths (1 <= M <= 64, any N, K % 32 == 0):
+// mma.sync m16n8k32 with register accumulators (q8_mmq.cuh), same inputs and
+// result as mma_linear.
+constexpr int kMmqMaxM = 64;
+int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
+               int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream,
+               const MmaScratch* scratch = nullptr);
+void mmq_split_needs(DeviceState* ds, int64_t N, int64_t K, int64_t M, size_t* part_bytes,
+                     int64_t* counters);
 
 // Mp for a given M (row pitch of dxT).
 inline int64_t mma_scale_pitch(int64_t M) { return (M + 3) / 4 * 4; }

@@ -226,11 +226,13 @@ def block_dots(weight: Q8Weight, xq: torch.Tensor) -> torch.Tensor:
     return out
 
 
-PATHS = {_lib.AXQ8_PATH_GEMV: "gemv", _lib.AXQ8_PATH_TENSOR_CORE: "tensor_core"}
+PATHS = {_lib.AXQ8_PATH_GEMV: "gemv", _lib.AXQ8_PATH_TENSOR_CORE: "tensor_core",
+         _lib.AXQ8_PATH_SKINNY: "skinny"}
 
 
 def linear_path(weight: Q8Weight, M: int, act_mode: str = "q8") -> str:
-    """Which kernel linear_from_gguf runs at M rows: "gemv" or "tensor_core"."""
+    """Which kernel linear_from_gguf runs at M rows: "gemv", "skinny" (decode
+    widths) or "tensor_core" (tcgen05)."""
     rc = _lib.load().axq8_linear_path(weight.c, M, ACT_MODES[act_mode])
     if rc < 0:
         check(rc)
@@ -270,6 +272,23 @@ def linear_q8act_t(weight: Q8Weight, xq: torch.Tensor, dxT: torch.Tensor,
     res = residual.contiguous() if residual is not None else None
     with torch.cuda.device(xq.device):
         check(_lib.load().axq8_linear_q8act_t(weight.c, C.c_void_p(xq.data_ptr()),
+                                              C.c_void_p(dxT.data_ptr()), M,
+                                              C.c_void_p(_ptr(res)) if res is not None else None,
+                                              C.c_void_p(out.data_ptr()), C.c_void_p(_stream())))
+    return out
+
+
+def linear_q8act_s(weight: Q8Weight, xq: torch.Tensor, dxT: torch.Tensor,
+                   residual: torch.Tensor | None = None) -> torch.Tensor:
+    """Skinny tensor-core product (1 <= M <= 64), same inputs as linear_q8act_t."""
+    _require_cuda(xq, "xq")
+    M = xq.shape[0]
+    if xq.shape[1] != weight.K:
+        raise RuntimeError("linear_from_gguf dimension mismatch: input K != weight K")
+    out = torch.empty(M, weight.N, dtype=torch.float32, device=xq.device)
+    res = residual.contiguous() if residual is not None else None
+    with torch.cuda.device(xq.device):
+        check(_lib.load().axq8_linear_q8act_s(weight.c, C.c_void_p(xq.data_ptr()),
                                               C.c_void_p(dxT.data_ptr()), M,
                                               C.c_void_p(_ptr(res)) if res is not None else None,
                                               C.c_void_p(out.data_ptr()), C.c_void_p(_stream())))

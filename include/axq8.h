@@ -91,18 +91,27 @@ int axq8_quantize_act(const float* x, int64_t M, int64_t K, int8_t* xq, float* d
  * the quantized activations live in a per-device workspace that this
  * library allocates on first use and grows when a larger M*K arrives (the
  * only allocation on this path); calls on different streams of one device
- * must not overlap.  A8 with M >= 32, N >= 128 and K % 128 == 0 runs the
- * tensor-core product (tcgen05 kind::i8, axq8_linear_q8act_t); everything
- * else runs the streaming GEMV kernel (axq8_linear_path tells which). */
+ * must not overlap.  A8 with 8 < M <= 32 runs the skinny tensor-core product
+ * (axq8_linear_q8act_s), A8 with M > 32, N >= 128 and K % 128 == 0 the tcgen05
+ * product (axq8_linear_q8act_t), other A8 shapes up to M = 64 the skinny one;
+ * everything else the streaming GEMV kernel (axq8_linear_path tells which). */
 int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int act_mode,
                 void* stream);
 
-/* Which kernel axq8_linear runs for w at M rows in act_mode. */
+/* Which kernel axq8_linear runs for w at M rows in act_mode (see above). */
 enum {
     AXQ8_PATH_GEMV = 0,
-    AXQ8_PATH_TENSOR_CORE = 1
+    AXQ8_PATH_TENSOR_CORE = 1,
+    AXQ8_PATH_SKINNY = 2
 };
 int axq8_linear_path(const axq8_weight_t* w, int64_t M, int act_mode);
+
+/* The same product for decode widths (1 <= M <= 64, any N, K % 32 == 0) with
+ * mma.sync m16n8k32 int8 and register accumulators (linear_from_gguf,
+ * linear.cpp:27-71, for batched decode); inputs from axq8_quantize_act_t.
+ * Exact int32 block dots; fp32 combination acc += (D_b*dw)*dx per block. */
+int axq8_linear_q8act_s(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
+                        const float* residual, float* y, void* stream);
 
 /* A8 quantization for the tensor-core product: xq[M, K] int8 as
  * axq8_quantize_act, the scales transposed: dxT[K/32, Mp] fp32 with

@@ -97,6 +97,9 @@ def test_tensor_core_entry_points_validate_shapes():
     assert rc == _lib.AXQ8_ERR_UNSUPPORTED
     w.K, w.row_stride = 256, lib.axq8_row_stride(256)
     assert lib.axq8_linear_path(ctypes.byref(w), 1, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_GEMV
+    assert lib.axq8_linear_path(ctypes.byref(w), 32, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_SKINNY
     assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_TENSOR_CORE
+    rc = lib.axq8_linear_q8act_s(ctypes.byref(w), 4096, 4096, 65, None, 4096, None)
+    assert rc == _lib.AXQ8_ERR_UNSUPPORTED and b"M <= 64" in lib.axq8_last_error()
     assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_F32) == _lib.AXQ8_PATH_GEMV
     assert lib.axq8_quantize_act_t(None, 4, 33, None, None, None) == _lib.AXQ8_ERR_INVALID

@@ -10,6 +10,7 @@ prefill / batched-decode path of axq8_linear) with the oracle.
   dequantized activation x' <= 1e-3 (REL_TOL).
 * Shapes cover ragged M and N tiles, every BN (32/64/128), split-K, and
   deterministic results across calls.
+* The skinny decode-width product (mma.sync, M <= 64) to the same bar.
 """
 from __future__ import annotations
 
@@ -83,8 +84,9 @@ def test_tensor_core_linear_vs_oracle(cuda, oracle, N, K, M):
     ops = _ops()
     blocks, x, w = _case(oracle, N, K, M, seed=7 * N + M)
     xt = torch.from_numpy(x).cuda()
-    assert ops.linear_path(w, M) == "tensor_core"
-    y = ops.linear_from_gguf(xt, w).cpu().numpy()
+    assert ops.linear_path(w, M) == ("skinny" if M <= 32 else "tensor_core")
+    xq, dxT = ops.quantize_activations_t(xt)
+    y = ops.linear_q8act_t(w, xq, dxT).cpu().numpy()      # the tcgen05 product at every M
     oq, od = oracle.quantize_act(x)
     ref = oracle.linear_a8(blocks, N, K, oq, od)
     xd = _xdeq(oq, od)
@@ -99,11 +101,12 @@ def test_tensor_core_linear_vs_oracle(cuda, oracle, N, K, M):
     assert ops.status() == 0
 
 
-def test_tensor_core_entry_points_agree(cuda, oracle):
-    """axq8_linear (A8, M >= 32) == axq8_linear_q8act_t bit for bit; the
+@pytest.mark.parametrize("M", [65, 300])
+def test_tensor_core_entry_points_agree(cuda, oracle, M):
+    """axq8_linear (A8, M > 64) == axq8_linear_q8act_t bit for bit; the
     residual is one fp32 add; repeated calls (split-K) are deterministic."""
     ops = _ops()
-    N, K, M = 1024, 4096, 48
+    N, K = 1024, 4096
     blocks, x, w = _case(oracle, N, K, M, seed=3)
     xt = torch.from_numpy(x).cuda()
     y1 = ops.linear_from_gguf(xt, w)
@@ -117,12 +120,48 @@ def test_tensor_core_entry_points_agree(cuda, oracle):
     assert ops.status() == 0
 
 
-def test_small_m_stays_on_gemv(cuda, oracle):
+# (N, K, M): one 8-row tile to all eight, ragged 16-row tiles, split-K over
+# CTAs (few tiles, long K) and over the warps only
+SKINNY = [(200, 1024, 1), (257, 512, 5), (1000, 4096, 9), (768, 4096, 16), (4096, 512, 31),
+          (2048, 5632, 33), (128, 14336, 64), (6144, 4096, 64)]
+
+
+@pytest.mark.parametrize("N,K,M", SKINNY)
+def test_skinny_product_vs_oracle(cuda, oracle, N, K, M):
+    """The decode-width product (mma.sync m16n8k32, register accumulators):
+    against the oracle's A8 linear within the combination tolerance, equal to
+    axq8_linear for 8 < M <= 64, deterministic, residual = one fp32 add."""
+    ops = _ops()
+    blocks, x, w = _case(oracle, N, K, M, seed=11 * N + M)
+    xt = torch.from_numpy(x).cuda()
+    xq, dxT = ops.quantize_activations_t(xt)
+    y = ops.linear_q8act_s(w, xq, dxT)
+    assert torch.equal(y, ops.linear_q8act_s(w, xq, dxT))
+    oq, od = oracle.quantize_act(x)
+    ref = oracle.linear_a8(blocks, N, K, oq, od)
+    xd = _xdeq(oq, od)
+    wdeq = oracle.dequant(blocks, N * K).reshape(N, K)
+    scale = np.abs(xd.astype(np.float64)) @ np.abs(wdeq.astype(np.float64)).T
+    err = rel_err(y.cpu().numpy(), ref.astype(np.float64), scale)
+    print(f"skinny [{N}x{K}] M={M}: err vs oracle {err:.2e}")
+    assert err <= A8_COMBINE_TOL
+    if ops.linear_path(w, M) == "skinny":
+        assert torch.equal(ops.linear_from_gguf(xt, w), y)
+    res = torch.randn(M, N, device="cuda")
+    assert torch.equal(ops.linear_q8act_s(w, xq, dxT, residual=res), res + y)
+    assert ops.status() == 0
+
+
+def test_dispatch_by_width(cuda, oracle):
     ops = _ops()
     _, _, w = _case(oracle, 256, 256, 1, seed=0)
     assert ops.linear_path(w, 1) == "gemv"
-    assert ops.linear_path(w, 31) == "gemv"
-    assert ops.linear_path(w, 32) == "tensor_core"
+    assert ops.linear_path(w, 8) == "gemv"
+    assert ops.linear_path(w, 9) == "skinny"
+    assert ops.linear_path(w, 32) == "skinny"
+    assert ops.linear_path(w, 33) == "tensor_core"
+    assert ops.linear_path(w, 65) == "tensor_core"
     assert ops.linear_path(w, 64, "f32") == "gemv"
     _, _, w2 = _case(oracle, 64, 256, 1, seed=0)
     assert ops.linear_path(w2, 256) == "gemv"        # N < 128
+    assert ops.linear_path(w2, 40) == "skinny"       # any N
