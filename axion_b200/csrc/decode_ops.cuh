@@ -47,22 +47,81 @@ __global__ void embed_kernel(const uint8_t* __restrict__ rows, int64_t rs, int H
 }
 
 // ---- RMSNorm (+ A8 quantization) ------------------------------------------------
-// One CTA per row.  out = (x * (1/sqrt(mean(x^2) + eps))) * w with the
-// reference's separately rounded operations; the sum of squares is a fixed
-// tree (warp sums, then warps in order), not the reference's sequential sum.
+// A8 quantization of one 32-block held by 4 consecutive lanes, 8 values each
+// (lane 4k + i holds elements 8i..8i+7): the 8 quants go to q, the scale to *d
+// from the group's first lane.  Bit-identical to quant_block_warp.  Every lane
+// of the warp calls it (full-mask shuffles); `valid` only gates the stores.
+__device__ __forceinline__ void quant_block_quad(const float (&v)[8], int lane, bool valid,
+                                                 int8_t* q, float* d) {
+    uint32_t ab = 0;
+#pragma unroll
+    for (int e = 0; e < 8; e++) ab = max(ab, __float_as_uint(fabsf(v[e])));
+    ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 1));
+    ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 2));
+    const float amax = __uint_as_float(ab);
+    const float id = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+    uint32_t lo = 0, hi = 0;
+#pragma unroll
+    for (int e = 0; e < 4; e++) {
+        lo |= (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[e], id)) << (8 * e);
+        hi |= (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[e + 4], id)) << (8 * e);
+    }
+    if (!valid) return;
+    *reinterpret_cast<uint2*>(q) = make_uint2(lo, hi);
+    if ((lane & 3) == 0) *d = __fdiv_rn(amax, 127.0f);
+}
+
+__device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
+    const float4 a = *reinterpret_cast<const float4*>(p);
+    const float4 b = *reinterpret_cast<const float4*>(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
+__device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
+    *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
+    *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
+}
+
+// One CTA per row, 8 consecutive elements per thread and up to kNormUnits such
+// units per thread, all held in registers (one read of x, loads in flight
+// together; the norm weight is read before the wait on the producer).
+// out = (x * (1/sqrt(mean(x^2) + eps))) * w with the reference's separately
+// rounded operations; the sum of squares is a fixed tree (per thread, warp
+// sums, then warps in order), not the reference's sequential sum.  H % 32 == 0,
+// H <= 8 * kNormUnits * blockDim.x, blockDim.x a multiple of 32.
 // dxt > 0: the block scales go transposed, dx[b * dxt + m] (the tensor-core
 // product's layout), else row-major dx[m * H/32 + b].  Same below.
+constexpr int kNormUnits = 4;
 template <bool Q8>
-__global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restrict__ w, int H,
-                               float eps, float* __restrict__ out, int8_t* __restrict__ xq,
-                               float* __restrict__ dx, int dxt) {
+__global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__ x,
+                                                       const float* __restrict__ w, int H,
+                                                       float eps, float* __restrict__ out,
+                                                       int8_t* __restrict__ xq,
+                                                       float* __restrict__ dx, int dxt) {
     __shared__ float red[32];
+    const int m = blockIdx.x, nu = H / 8;
+    float wv[kNormUnits][8], v[kNormUnits][8];
+#pragma unroll
+    for (int u = 0; u < kNormUnits; u++) {
+        const int j = threadIdx.x + u * blockDim.x;
+        if (j < nu) load8(w + 8 * j, wv[u]);
+    }
     pdl_launch_dependents();
     pdl_wait();
-    const int m = blockIdx.x;
     const float* xr = x + (int64_t)m * H;
     float s = 0.0f;
-    for (int k = threadIdx.x; k < H; k += blockDim.x) s = fmaf(xr[k], xr[k], s);
+#pragma unroll
+    for (int u = 0; u < kNormUnits; u++) {
+        const int j = threadIdx.x + u * blockDim.x;
+        if (j < nu) {
+            load8(xr + 8 * j, v[u]);
+        } else {
+#pragma unroll
+            for (int e = 0; e < 8; e++) v[u][e] = wv[u][e] = 0.0f;
+        }
+#pragma unroll
+        for (int e = 0; e < 8; e++) s = fmaf(v[u][e], v[u][e], s);
+    }
     s = warp_sum(s);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
     if (lane == 0) red[warp] = s;
@@ -75,18 +134,31 @@ __global__ void rmsnorm_kernel(const float* __restrict__ x, const float* __restr
     __syncthreads();
     const float ms = __fdiv_rn(red[0], (float)H);
     const float inv = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(ms, eps)));
-    if (!Q8) {
-        for (int k = threadIdx.x; k < H; k += blockDim.x)
-            out[(int64_t)m * H + k] = __fmul_rn(__fmul_rn(xr[k], inv), w[k]);
-    } else {
-        const int nb = H / QK;
-        for (int b = warp; b < nb; b += nw) {
-            const int k = b * QK + lane;
-            const float v = __fmul_rn(__fmul_rn(xr[k], inv), w[k]);
-            quant_block_warp(v, lane, xq + (int64_t)m * H + b * QK,
+    const int nb = H / QK;
+#pragma unroll
+    for (int u = 0; u < kNormUnits; u++) {
+        const int j = threadIdx.x + u * blockDim.x;
+        if (u * blockDim.x >= (unsigned)nu) break;   // uniform over the CTA
+#pragma unroll
+        for (int e = 0; e < 8; e++) v[u][e] = __fmul_rn(__fmul_rn(v[u][e], inv), wv[u][e]);
+        if (!Q8) {
+            if (j < nu) store8(out + (int64_t)m * H + 8 * j, v[u]);
+        } else {
+            const int b = j >> 2;
+            quant_block_quad(v[u], lane, j < nu, xq + (int64_t)m * H + 8 * j,
                              dx + (dxt ? (int64_t)b * dxt + m : (int64_t)m * nb + b));
         }
     }
+}
+
+// Threads of an rmsnorm_kernel CTA for rows of H: two 8-element units per
+// thread where that fits in 1024 threads; 0 when H is beyond the kernel.
+inline int rmsnorm_threads(int H) {
+    if (H <= 0 || H % QK) return 0;
+    const int nu = H / 8;
+    const int t = ((nu + 1) / 2 + 31) / 32 * 32;
+    if (t <= 1024) return t;
+    return nu <= 1024 * kNormUnits ? 1024 : 0;
 }
 
 // The split merge of one query head (one warp): out = sum_s acc_s e^(m_s - M)
@@ -701,26 +773,34 @@ __global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key,
 
 // ---- SiLU(gate) * up (+ A8 quantization) -------------------------------------------
 // gu row = [gate (F) | up (F)].  a = (g / (1 + e^-g)) * u, rounded per op as
-// silu.cpp and elementwise.cpp do.  One warp per 32-block.
+// silu.cpp and elementwise.cpp do.  8 consecutive elements per thread (4
+// threads per 32-block); F % 32 == 0.
 template <bool Q8>
 __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
                                 float* __restrict__ out, int8_t* __restrict__ xq,
                                 float* __restrict__ dx, int dxt) {
     pdl_launch_dependents();
     pdl_wait();
-    const int nb = F / QK;
-    const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int nu = F / 8, nb = F / QK;
+    const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     const int lane = threadIdx.x & 31;
-    if (gw >= M * nb) return;
-    const int m = gw / nb, b = gw % nb;
-    const int i = b * QK + lane;
-    const float g = gu[(int64_t)m * 2 * F + i];
-    const float u = gu[(int64_t)m * 2 * F + F + i];
-    const float a = __fmul_rn(__fdiv_rn(g, __fadd_rn(1.0f, expf(-g))), u);
-    if (!Q8) {
-        out[(int64_t)m * F + i] = a;
+    const bool valid = j < (int64_t)M * nu;
+    const int m = valid ? (int)(j / nu) : 0, c = valid ? (int)(j % nu) : 0;
+    float g[8], u[8], a[8];
+    if (valid) {
+        load8(gu + (int64_t)m * 2 * F + 8 * c, g);
+        load8(gu + (int64_t)m * 2 * F + F + 8 * c, u);
     } else {
-        quant_block_warp(a, lane, xq + (int64_t)m * F + b * QK,
+#pragma unroll
+        for (int e = 0; e < 8; e++) g[e] = u[e] = 0.0f;
+    }
+#pragma unroll
+    for (int e = 0; e < 8; e++) a[e] = __fmul_rn(__fdiv_rn(g[e], __fadd_rn(1.0f, expf(-g[e]))), u[e]);
+    if (!Q8) {
+        if (valid) store8(out + (int64_t)m * F + 8 * c, a);
+    } else {
+        const int b = c >> 2;
+        quant_block_quad(a, lane, valid, xq + (int64_t)m * F + 8 * c,
                          dx + (dxt ? (int64_t)b * dxt + m : (int64_t)m * nb + b));
     }
 }

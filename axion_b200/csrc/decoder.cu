@@ -45,8 +45,6 @@ using namespace axq8;
 
 namespace {
 
-constexpr int kNormThreads = 256;
-
 struct Layer {
     uint8_t* qkv = nullptr;    // [Nq + 2 Nkv, H] Q8R
     uint8_t* o = nullptr;      // [H, Nq]
@@ -334,16 +332,24 @@ int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s, int dxt) 
 int launch_rmsnorm(axdec_model* m, int M, const float* x, const float* w, cudaStream_t s,
                    int dxt = 0) {
     const axdec_config_t& c = m->c;
+    const int threads = rmsnorm_threads(c.hidden);   // checked at create
     if (c.act_mode == AXQ8_ACT_F32) {
-        AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<false>, dim3(M), dim3(kNormThreads), 0, s, true, x, w,
+        AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<false>, dim3(M), dim3(threads), 0, s, true, x, w,
                                c.hidden, c.rms_eps, m->x32, (int8_t*)nullptr, (float*)nullptr, 0),
                       "rmsnorm launch");
     } else {
-        AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<true>, dim3(M), dim3(kNormThreads), 0, s, true, x, w,
+        AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<true>, dim3(M), dim3(threads), 0, s, true, x, w,
                                c.hidden, c.rms_eps, (float*)nullptr, m->xq, m->dx, dxt),
                       "rmsnorm launch");
     }
     return AXQ8_OK;
+}
+
+// Grid of silu_mul_kernel for M rows of F (8 elements per thread).
+constexpr int kSiluThreads = 256;
+inline dim3 silu_grid(int M, int F) {
+    const int64_t units = (int64_t)M * (F / 8);
+    return dim3((unsigned)((units + kSiluThreads - 1) / kSiluThreads));
 }
 
 // Whether a step of M sequences runs wide: A8, M >= kWideMinM (the fused
@@ -365,19 +371,23 @@ bool wide_step(const axdec_model* m, int M) {
            mma_shape_ok(2 * F, H, M) && mma_shape_ok(H, F, M) && mma_shape_ok(c.vocab, H, M);
 }
 
-// Widths up to which wide steps prefer the skinny product (AXDEC_SKINNY_M
-// overrides the library default of 32, up to 64, for tuning).
-int skinny_prefer_m() {
+// Whether a wide step's linear of [N, K] at M rows takes the skinny product:
+// the library's shape rule (skinny_preferred), or AXDEC_SKINNY_M = w (0..64)
+// for a plain width threshold (tuning runs).
+int skinny_m_override() {
     static const int v = [] {
         const char* e = getenv("AXDEC_SKINNY_M");
-        const int x = e ? atoi(e) : kMmqPreferM;
-        return x >= 0 && x <= kMmqMaxM ? x : kMmqPreferM;
+        const int x = e ? atoi(e) : -1;
+        return x >= 0 && x <= kMmqMaxM ? x : -1;
     }();
     return v;
 }
 
 bool use_skinny(int64_t N, int64_t K, int M) {
-    return M <= skinny_prefer_m() || (M <= kMmqMaxM && !mma_shape_ok(N, K, M));
+    if (M > kMmqMaxM) return false;
+    if (!mma_shape_ok(N, K, M)) return true;
+    const int o = skinny_m_override();
+    return o >= 0 ? M <= o : skinny_preferred(N, M);
 }
 
 int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
@@ -388,7 +398,7 @@ int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M
     w.K = K;
     w.row_stride = q8r_row_stride(K);
     w.device = m->ds->device;
-    if (use_skinny(N, K, M)) return mmq_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, s, &m->mma_sc);
+    if (use_skinny(N, K, M)) return mmq_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, s);
     return mma_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, nullptr, s, &m->mma_sc);
 }
 
@@ -425,8 +435,7 @@ int launch_step_wide(axdec_model* m, int M, cudaStream_t s) {
         if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
         if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s, dxt))) return rc;
         if ((rc = wide_linear(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu, s))) return rc;
-        const int nwarps = M * (F / QK);
-        AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0, s, true,
+        AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, silu_grid(M, F), dim3(kSiluThreads), 0, s, true,
                                (const float*)m->gu, F, M, (float*)nullptr, m->xq, m->dx, dxt),
                       "silu launch");
         if ((rc = wide_linear(m, Ly.down, H, F, M, resid, m->h, s))) return rc;
@@ -525,15 +534,14 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
             a.src = m->gu;
             rc = gemv_launch_mt<PRO_SILU, EPI_STORE, float>(ds, a, s);
         } else {
-            const int nwarps = M * (F / QK);
             if (a32) {
-                AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, dim3((nwarps + 7) / 8), dim3(256), 0,
+                AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, silu_grid(M, F), dim3(kSiluThreads), 0,
                                        s, true, (const float*)m->gu, F, M, m->x32,
                                        (int8_t*)nullptr, (float*)nullptr, 0),
                               "silu launch");
                 rc = gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s);
             } else {
-                AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, dim3((nwarps + 7) / 8), dim3(256), 0,
+                AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, silu_grid(M, F), dim3(kSiluThreads), 0,
                                        s, true, (const float*)m->gu, F, M, (float*)nullptr, m->xq,
                                        m->dx, 0),
                               "silu launch");
@@ -693,6 +701,9 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
         return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: head_dim %d (32, 64, 128 supported)",
                     c.head_dim);
     if (c.kv_block != 16) return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: kv_block must be 16");
+    if (!rmsnorm_threads(c.hidden))
+        return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: hidden %d above the norm kernel's %d",
+                    c.hidden, 8 * kNormUnits * 1024);
     if (c.n_heads / c.n_kv_heads > 16)
         return fail(AXQ8_ERR_UNSUPPORTED, "axdec_create: more than 16 query heads per kv head");
     if (c.act_mode != AXQ8_ACT_Q8 && c.act_mode != AXQ8_ACT_F32)
@@ -772,9 +783,7 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
             for (auto& sh : shapes) {
                 size_t pb = 0;
                 int64_t cn = 0;
-                if (use_skinny(sh[0], sh[1], mm))
-                    mmq_split_needs(ds, sh[0], sh[1], mm, &pb, &cn);
-                else if (mma_shape_ok(sh[0], sh[1], mm))
+                if (!use_skinny(sh[0], sh[1], mm) && mma_shape_ok(sh[0], sh[1], mm))
                     mma_split_needs(ds, sh[0], sh[1], mm, &pb, &cn);
                 part = std::max(part, pb);
                 cnt = std::max(cnt, cn);

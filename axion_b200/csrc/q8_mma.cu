@@ -111,7 +111,7 @@ int launch_bn(DeviceState* ds, const CUtensorMap& tw, const CUtensorMap& tx, con
 
 bool skinny_eligible(const axq8_weight_t* w, int64_t M) {
     if (!w || M <= 8 || M > kMmqMaxM || w->K % QK || w->K > (1 << 24)) return false;
-    return M <= kMmqPreferM || !mma_eligible(w, M);
+    return skinny_preferred(w->N, M) || !mma_eligible(w, M);
 }
 
 bool mma_eligible(const axq8_weight_t* w, int64_t M) {
@@ -225,33 +225,38 @@ MmqPlan mmq_plan(DeviceState* ds, int64_t N, int64_t K, int64_t M) {
     const int64_t want = 2 * (int64_t)ds->sm_count;   // two CTAs per SM
     int splits = (int)std::max<int64_t>(1, (want + p.tiles - 1) / p.tiles);
     splits = std::min(splits, std::max(1, nch / 2));   // >= two chunks per split
+    splits = std::min(splits, kMmqMaxSplits);          // one cluster per row tile
     p.per = (nch + splits - 1) / splits;
     p.splits = (nch + p.per - 1) / p.per;
     return p;
 }
 template <int MT8>
 int mmq_launch(const MmqArgs& a, dim3 grid, cudaStream_t s) {
-    AXQ8_CUDA_TRY(launch_k(q8_mmq_kernel<MT8>, grid, dim3(kMmqWarps * 32), 0, s, true, a),
-                  "q8_mmq launch");
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = dim3(kMmqWarps * 32);
+    cfg.stream = s;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeClusterDimension;
+    attr[1].val.clusterDim.x = 1;
+    attr[1].val.clusterDim.y = grid.y;
+    attr[1].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = grid.y > 1 ? 2 : 1;
+    AXQ8_CUDA_TRY(cudaLaunchKernelEx(&cfg, q8_mmq_kernel<MT8>, a), "q8_mmq launch");
     return AXQ8_OK;
 }
 }  // namespace
 
-void mmq_split_needs(DeviceState* ds, int64_t N, int64_t K, int64_t M, size_t* part_bytes,
-                     int64_t* counters) {
-    const MmqPlan p = mmq_plan(ds, N, K, M);
-    *part_bytes = p.splits > 1 ? sizeof(float) * (size_t)p.splits * M * N : 0;
-    *counters = p.splits > 1 ? p.tiles : 0;
-}
-
 int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
-               int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream,
-               const MmaScratch* scratch) {
+               int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream) {
     if (!w || M < 1 || M > kMmqMaxM || w->K % QK || w->K > (1 << 24) || w->N > (1 << 30) ||
         !xq || !dxT || !y || ldy < w->N)
         return fail(AXQ8_ERR_INVALID, "skinny linear: unsupported arguments");
     const MmqPlan plan = mmq_plan(ds, w->N, w->K, M);
-    if (plan.tiles > 65535 * 32) return fail(AXQ8_ERR_UNSUPPORTED, "skinny linear: N too large");
+    if (plan.tiles > 0x7fffffff) return fail(AXQ8_ERR_UNSUPPORTED, "skinny linear: N too large");
     MmqArgs a = {};
     a.rows = static_cast<const uint8_t*>(w->rows);
     a.row_stride = w->row_stride;
@@ -265,20 +270,6 @@ int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const 
     a.residual = residual;
     a.y = y;
     a.ldy = (int)ldy;
-    if (plan.splits > 1) {
-        const size_t need = sizeof(float) * (size_t)plan.splits * M * w->N;
-        if (scratch) {
-            if (scratch->part_bytes < need || scratch->counter_slots < plan.tiles)
-                return fail(AXQ8_ERR_INVALID, "skinny linear: caller scratch too small");
-            a.part = scratch->part;
-            a.counters = scratch->counters;
-        } else {
-            if (plan.tiles > kCounterSlots)
-                return fail(AXQ8_ERR_UNSUPPORTED, "skinny linear: too many split tiles");
-            int rc = split_scratch(ds, need, &a.part, &a.counters);
-            if (rc) return rc;
-        }
-    }
     const dim3 grid((unsigned)plan.tiles, (unsigned)plan.splits);
     if (M <= 8) return mmq_launch<1>(a, grid, stream);
     if (M <= 16) return mmq_launch<2>(a, grid, stream);

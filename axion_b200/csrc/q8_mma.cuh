@@ -331,6 +331,7 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
                 const uint32_t wsel = ((k4 & 2) ? w23 : w01) >> ((k4 & 1) * 16);
                 const float dw = __half2float(__ushort_as_half((unsigned short)(wsel & 0xFFFFu)));
                 const float ncw = -kMagic * dw;
+                const float2 dw2 = make_float2(dw, dw), ncw2 = make_float2(ncw, ncw);
                 if (!__all_sync(0xffffffffu, wait_or_flag(&tfull[k4], i & 1, a.status, abort))) {
                     ok = false;
                     break;
@@ -354,10 +355,12 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
                     for (int j = 0; j < 16; j += 4) {
                         const float4 d4 = *reinterpret_cast<const float4*>(dxs + k4 * BN + c * 16 + j);
                         const int jj = (c * 16 + j) / 2;
-                        acc[jj].x = fmaf(fmaf(__uint_as_float(cur[j]), dw, ncw), d4.x, acc[jj].x);
-                        acc[jj].y = fmaf(fmaf(__uint_as_float(cur[j + 1]), dw, ncw), d4.y, acc[jj].y);
-                        acc[jj + 1].x = fmaf(fmaf(__uint_as_float(cur[j + 2]), dw, ncw), d4.z, acc[jj + 1].x);
-                        acc[jj + 1].y = fmaf(fmaf(__uint_as_float(cur[j + 3]), dw, ncw), d4.w, acc[jj + 1].y);
+                        const float2 t0 = ffma2(make_float2(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])),
+                                                dw2, ncw2);
+                        const float2 t1 = ffma2(make_float2(__uint_as_float(cur[j + 2]), __uint_as_float(cur[j + 3])),
+                                                dw2, ncw2);
+                        acc[jj] = ffma2(t0, make_float2(d4.x, d4.y), acc[jj]);
+                        acc[jj + 1] = ffma2(t1, make_float2(d4.z, d4.w), acc[jj + 1]);
                     }
                     if (DOTS && n < a.N) {
                         const int nb = a.K / QK;
@@ -409,14 +412,30 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
             asm volatile("bar.sync 1, %0;" ::"n"(EW * 32) : "memory");
             if (*last_flag && n < a.N) {
                 __threadfence();
-                for (int j = 0; j < CW; j++) {
-                    const int m = m0 + half * CW + j;
-                    if (m >= a.M) break;
-                    float v = 0.0f;
-                    for (int z = 0; z < splits; z++)
-                        v = __fadd_rn(v, __ldcg(a.part + ((int64_t)z * a.M + m) * a.N + n));
-                    const int64_t o = (int64_t)m * a.ldy + n;
-                    a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+                // the thread's CW outputs in batches of 16: each split's 16
+                // loads are in flight together, the adds stay in split order
+#pragma unroll
+                for (int j0 = 0; j0 < CW; j0 += 16) {
+                    const int mb = m0 + half * CW + j0;
+                    if (mb >= a.M) break;
+                    float v[16];
+#pragma unroll
+                    for (int j = 0; j < 16; j++) v[j] = 0.0f;
+                    for (int z = 0; z < splits; z++) {
+                        const float* pz2 = a.part + ((int64_t)z * a.M + mb) * a.N + n;
+                        float p[16];
+#pragma unroll
+                        for (int j = 0; j < 16; j++)
+                            p[j] = mb + j < a.M ? __ldcg(pz2 + (int64_t)j * a.N) : 0.0f;
+#pragma unroll
+                        for (int j = 0; j < 16; j++) v[j] = __fadd_rn(v[j], p[j]);
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; j++) {
+                        if (mb + j >= a.M) break;
+                        const int64_t o = (int64_t)(mb + j) * a.ldy + n;
+                        a.y[o] = a.residual ? __fadd_rn(a.residual[o], v[j]) : v[j];
+                    }
                 }
             }
         }

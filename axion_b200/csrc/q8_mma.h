@@ -18,12 +18,20 @@ constexpr int kMmaMinM = 32;
 // N >= 128, K a multiple of 128.
 bool mma_eligible(const axq8_weight_t* w, int64_t M);
 
-// Widths up to which the skinny product is preferred where both apply (the
-// tcgen05 product is faster from 33 rows on large weights, measured).
+// Widths up to which the skinny product is preferred for every shape, and
+// the row count up to which it is preferred from there to kMmqMaxM rows (the
+// tcgen05 product's fixed costs dominate small weights; measured on B200 at
+// 64 rows: skinny 8.7-16 us vs 14-34 us for N <= 4096, even at N = 6144-7168,
+// tcgen05 ahead from N = 14336).
+constexpr int kMmqMaxM = 64;
 constexpr int kMmqPreferM = 32;
+constexpr int64_t kMmqPreferN = 8192;
+inline bool skinny_preferred(int64_t N, int64_t M) {
+    return M <= kMmqPreferM || (M <= kMmqMaxM && N <= kMmqPreferN);
+}
 
-// Whether axq8_linear takes the skinny product for w at M rows: 8 < M <= 32,
-// or 32 < M <= 64 where the tcgen05 product does not tile the shape.
+// Whether axq8_linear takes the skinny product for w at M rows: 8 < M <= 64
+// where skinny_preferred holds or the tcgen05 product does not tile the shape.
 bool skinny_eligible(const axq8_weight_t* w, int64_t M);
 
 // Caller-owned split-K scratch (partials and per-tile counters, the counters
@@ -57,13 +65,9 @@ inline bool mma_shape_ok(int64_t N, int64_t K, int64_t M) {
 
 // Skinny product for decode widths (1 <= M <= 64, any N, K % 32 == 0):
 // mma.sync m16n8k32 with register accumulators (q8_mmq.cuh), same inputs and
-// result as mma_linear.
-constexpr int kMmqMaxM = 64;
+// result as mma_linear.  Its K splits combine on chip: no scratch.
 int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
-               int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream,
-               const MmaScratch* scratch = nullptr);
-void mmq_split_needs(DeviceState* ds, int64_t N, int64_t K, int64_t M, size_t* part_bytes,
-                     int64_t* counters);
+               int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream);
 
 // Mp for a given M (row pitch of dxT).
 inline int64_t mma_scale_pitch(int64_t M) { return (M + 3) / 4 * 4; }

@@ -24,13 +24,18 @@
 // (double buffered; 16-byte chunks XOR-swizzled by row so the 8-byte fragment
 // reads are conflict-free; rows past M and bytes past K zero-filled) and shared
 // by the 8 warps; each warp's weight fragments come straight from global
-// memory one chunk ahead.  A split launch writes partial tiles and its last
-// CTA (atomic counter, back to zero) adds them in split order: deterministic.
+// memory one chunk ahead.  The K splits of a row tile (blockIdx.y, at most 8)
+// run as one thread-block cluster: each CTA leaves its fp32 partial tile in
+// shared memory and, after a cluster barrier, every CTA adds one slice of the
+// tile over the cluster's partials in split order (distributed shared memory),
+// so the combine needs no global workspace and stays deterministic.
 #pragma once
 
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <cooperative_groups.h>
 
 #include "common.cuh"
 
@@ -39,6 +44,19 @@ namespace axq8 {
 constexpr int kMmqWarps = 8;
 constexpr int kMmqRows = 16 * kMmqWarps;   // weight rows per CTA
 constexpr int kMmqChunkKb = 4;             // 32-blocks per staged chunk (128 bytes of K)
+constexpr int kMmqMaxSplits = 8;           // cluster size limit (portable)
+
+// Shared memory of one CTA: the double-buffered activation chunk and scales
+// during the main loop, then (split launches) the fp32 partial tile [MR][kMmqTilePitch].
+constexpr int kMmqTilePitch = kMmqRows + 4;   // conflict-free fragment stores
+template <int MT8>
+struct MmqSmem {
+    static constexpr int MR = 8 * MT8;
+    static constexpr int XS = 2 * MR * kMmqChunkKb * 32;
+    static constexpr int DXS = 2 * kMmqChunkKb * MR * 4;
+    static constexpr int TILE = MR * kMmqTilePitch * 4;
+    static constexpr int BYTES = XS + DXS > TILE ? XS + DXS : TILE;
+};
 
 struct MmqArgs {
     const uint8_t* rows;     // repacked Q8R rows
@@ -51,8 +69,6 @@ struct MmqArgs {
     const float* residual;   // optional [M][ldy]
     float* y;                // [M][ldy]
     int ldy;
-    float* part;             // [splits][M][N] when gridDim.y > 1
-    int* counters;           // [gridDim.x]
 };
 
 __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a, uint32_t b0, uint32_t b1,
@@ -79,14 +95,16 @@ struct MmqWeights {
     uint2 s[2];
 };
 
+// Launched with cluster dimensions (1, gridDim.y, 1) when gridDim.y > 1.
 template <int MT8>   // 8-row activation tiles (M <= 8 * MT8)
 __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs a) {
     constexpr uint32_t kMagicBitsI = 0x4B400000u;   // 1.5 * 2^23 as fp32
     constexpr float kMagicF = 12582912.0f;
-    constexpr int MR = 8 * MT8;                     // staged activation rows
-    __shared__ __align__(16) uint8_t xs[2][MR][kMmqChunkKb * 32];
-    __shared__ __align__(16) float dxs[2][kMmqChunkKb][MR];
-    __shared__ int last;
+    using SM = MmqSmem<MT8>;
+    constexpr int MR = SM::MR;                      // staged activation rows
+    __shared__ __align__(16) uint8_t smem[SM::BYTES];
+    auto xs = reinterpret_cast<uint8_t(*)[MR][kMmqChunkKb * 32]>(smem);
+    auto dxs = reinterpret_cast<float(*)[kMmqChunkKb][MR]>(smem + SM::XS);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
     const int n0 = blockIdx.x * kMmqRows + warp * 16;
@@ -127,9 +145,9 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
             cp_async16_zfill(&dxs[buf][k4][r4], a.dxT + (ok ? (int64_t)kb * a.Mp + r4 : 0), ok);
         }
     };
-    float acc[MT8][4];
+    float2 acc[MT8][2];   // [j][0]: row g, columns 8j + 2t (+1); [j][1]: row g + 8
 #pragma unroll
-    for (int j = 0; j < MT8; j++) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+    for (int j = 0; j < MT8; j++) acc[j][0] = acc[j][1] = make_float2(0.0f, 0.0f);
     MmqWeights Wc, Wn;
     if (ch0 < ch1) load_w(ch0, Wc);          // weights are static: before the wait
     pdl_launch_dependents();
@@ -164,10 +182,12 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
                 const float2 dxv = *reinterpret_cast<const float2*>(&dxs[buf][k4][8 * j + 2 * t]);
                 int d[4];
                 mma_s8_16832(d, af, B.x, B.y, (int)kMagicBitsI);
-                acc[j][0] = fmaf(fmaf(__int_as_float(d[0]), dwa, nca), dxv.x, acc[j][0]);
-                acc[j][1] = fmaf(fmaf(__int_as_float(d[1]), dwa, nca), dxv.y, acc[j][1]);
-                acc[j][2] = fmaf(fmaf(__int_as_float(d[2]), dwb, ncb), dxv.x, acc[j][2]);
-                acc[j][3] = fmaf(fmaf(__int_as_float(d[3]), dwb, ncb), dxv.y, acc[j][3]);
+                const float2 ta = ffma2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])),
+                                        make_float2(dwa, dwa), make_float2(nca, nca));
+                const float2 tb = ffma2(make_float2(__int_as_float(d[2]), __int_as_float(d[3])),
+                                        make_float2(dwb, dwb), make_float2(ncb, ncb));
+                acc[j][0] = ffma2(ta, dxv, acc[j][0]);
+                acc[j][1] = ffma2(tb, dxv, acc[j][1]);
             }
         }
         Wc = Wn;
@@ -176,41 +196,58 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
     if (ch0 >= ch1) cp_async_wait_all();
     // outputs: rows n0 + g (+8), columns 8j + 2t (+1)
     const int splits = gridDim.y;
-    float* dst = splits == 1 ? a.y : a.part + (int64_t)blockIdx.y * a.M * a.N;
-    const int ld = splits == 1 ? a.ldy : a.N;
+    if (splits == 1) {
+#pragma unroll
+        for (int j = 0; j < MT8; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int n = n0 + g + ((e & 2) ? 8 : 0);
+                const int m = 8 * j + 2 * t + (e & 1);
+                if (n >= a.N || m >= a.M) continue;
+                const int64_t o = (int64_t)m * a.ldy + n;
+                const float v = (e & 1) ? acc[j][e >> 1].y : acc[j][e >> 1].x;
+                a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+            }
+        return;
+    }
+    // split launch: partial tile -> shared memory, then the cluster's combine
+    float* tile = reinterpret_cast<float*>(smem);   // [MR][kMmqTilePitch], over the stage buffers
+    __syncthreads();
 #pragma unroll
     for (int j = 0; j < MT8; j++)
 #pragma unroll
-        for (int e = 0; e < 4; e++) {
-            const int n = n0 + g + ((e & 2) ? 8 : 0);
-            const int m = 8 * j + 2 * t + (e & 1);
-            if (n >= a.N || m >= a.M) continue;
-            const int64_t o = (int64_t)m * ld + n;
-            float v = acc[j][e];
-            if (splits == 1 && a.residual) v = __fadd_rn(a.residual[o], v);
-            dst[o] = v;
-        }
-    if (splits == 1) return;
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        int* c = a.counters + blockIdx.x;
-        last = atomicAdd(c, 1) == splits - 1;
-        if (last) *c = 0;
-    }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
+        for (int e = 0; e < 4; e++)
+            tile[(8 * j + 2 * t + (e & 1)) * kMmqTilePitch + warp * 16 + g + ((e & 2) ? 8 : 0)] =
+                (e & 1) ? acc[j][e >> 1].y : acc[j][e >> 1].x;
+    namespace cg = cooperative_groups;
+    cg::cluster_group cluster = cg::this_cluster();
+    cluster.sync();
+    const float* peer[kMmqMaxSplits];
+#pragma unroll
+    for (int z = 0; z < kMmqMaxSplits; z++)
+        peer[z] = z < splits ? cluster.map_shared_rank(tile, z) : tile;
+    // this CTA's slice of the M x 128 outputs, in row-major (m, r) order
+    const int total = a.M * kMmqRows;
+    const int rank = (int)cluster.block_rank();
+    const int lo = (int)((int64_t)total * rank / splits), hi = (int)((int64_t)total * (rank + 1) / splits);
     const int nb0 = blockIdx.x * kMmqRows;
-    for (int idx = threadIdx.x; idx < kMmqRows * a.M; idx += blockDim.x) {
-        const int r = idx % kMmqRows, m = idx / kMmqRows;
-        const int n = nb0 + r;
-        if (n >= a.N) continue;
+    for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
+        const int m = i / kMmqRows, r = i % kMmqRows;
+        const int off = m * kMmqTilePitch + r;
+        float p[kMmqMaxSplits];
+#pragma unroll
+        for (int z = 0; z < kMmqMaxSplits; z++) p[z] = z < splits ? peer[z][off] : 0.0f;
         float v = 0.0f;
-        for (int z = 0; z < splits; z++) v = __fadd_rn(v, __ldcg(a.part + ((int64_t)z * a.M + m) * a.N + n));
-        const int64_t o = (int64_t)m * a.ldy + n;
-        a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+#pragma unroll
+        for (int z = 0; z < kMmqMaxSplits; z++)
+            if (z < splits) v = __fadd_rn(v, p[z]);
+        const int n = nb0 + r;
+        if (n < a.N) {
+            const int64_t o = (int64_t)m * a.ldy + n;
+            a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+        }
     }
+    cluster.sync();   // peers' tiles stay alive until every slice is read
 }
 
 }  // namespace axq8
