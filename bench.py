@@ -2,7 +2,7 @@
 """Benchmark of the B200 Q8_0 hot path; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl axion|reference]
-                    [--workload decode|gemv|prefill|llama3]
+                    [--workload decode|gemv|prefill|llama3|skinny]
 
 Workloads
   decode (default) TinyLlama-1.1B-architecture decode: 22
@@ -28,8 +28,15 @@ Workloads
          theta 5e5 (not given by the config; Llama-3's), batch 64, random
          2048-token prompts, then K (default 128) greedy steps; tensor parallel
          over the N GPUs of the run (strong scaling).  Every linear runs on the
-         tcgen05 kind::i8 product at M = 64.  Metric: decode tokens/s of the
-         whole job; the reference arm is extrapolated from one linear.
+         skinny or the tcgen05 product at M = 64 (by shape).  Metric: decode
+         tokens/s of the whole job; the reference arm is extrapolated from one
+         linear.
+  skinny the decode-width product (q8_mmq_kernel, mma.sync int8 with register
+         accumulators) on the Llama-3-8B layer shapes [6144x4096],
+         [4096x4096], [28672x4096], [4096x14336] at M = 16, 32, 64 with
+         pre-quantized activations.  One step = the 12 products.  Metric:
+         algorithmic bytes / s (weights once + activations + outputs); e2e runs
+         the public axq8_linear with host buffers.
   prefill Q8_0 prefill GEMM sweep: Llama-2-7B linear
          shapes [4096x4096], [11008x4096], [4096x11008], [32000x4096] x M in
          {256, 1024, 2048, 4096} on the tcgen05 kind::i8 path.  One step = one
@@ -675,6 +682,183 @@ def llama3_reference(args, rows: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
+# Decode-width products: the skinny Q8_0 x A8 kernel (q8_mmq_kernel) on the
+# Llama-3-8B layer shapes of the batched-decode workload, M = 16 / 32 / 64
+# ---------------------------------------------------------------------------
+
+SKINNY_SHAPES = [(6144, 4096), (4096, 4096), (28672, 4096), (4096, 14336)]
+SKINNY_MS = [16, 32, 64]
+SKINNY_METRIC = "Q8_0 decode-width product HBM GB/s (Llama-3-8B layer shapes, M=16/32/64)"
+SKINNY_CONFIG = {"workload": "q8_0_skinny_llama3_8b_layer_m16_32_64",
+                 "shapes": "[6144x4096] [4096x4096] [28672x4096] [4096x14336]",
+                 "M": SKINNY_MS}
+
+
+def skinny_bytes(N: int, K: int, M: int) -> int:
+    """Weights once (34-byte blocks), int8 activations + fp32 block scales, fp32 output."""
+    return N * (K // 32) * 34 + M * K + M * (K // 32) * 4 + M * N * 4
+
+
+def run_skinny_axion(args, d: Dist) -> dict:
+    """One step = the 12 products (every shape at every M, M outer), each
+    through axq8_linear_q8act_s (pre-quantized activations, the decode step's
+    form).  Between two uses of one weight the other three stream 100-200 MB,
+    more than L2, so every product reads its weight from HBM."""
+    import torch
+    from axion_b200 import _lib, ops
+    lib = _lib.load()
+    dev = torch.device("cuda", d.local)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    s_ptr = C.c_void_p(stream.cuda_stream)
+    g = torch.Generator(device=dev).manual_seed(77 + d.rank)
+    with torch.cuda.stream(stream):
+        ws = [ops.Q8Weight.synthetic(L3_SEED + i, N, K, device=dev)
+              for i, (N, K) in enumerate(SKINNY_SHAPES)]
+        acts = {}
+        for M in SKINNY_MS:
+            for K in sorted({k for _, k in SKINNY_SHAPES}):
+                x = torch.randn(M, K, generator=g, device=dev)
+                acts[(M, K)] = (x,) + tuple(ops.quantize_activations_t(x))
+        ys = {(M, N): torch.empty(M, N, device=dev) for M in SKINNY_MS for N, _ in SKINNY_SHAPES}
+    cases = [(M, i) for M in SKINNY_MS for i in range(len(SKINNY_SHAPES))]
+    step_bytes = sum(skinny_bytes(*SKINNY_SHAPES[i], M) for M, i in cases)
+
+    def product(M, i):
+        N, K = SKINNY_SHAPES[i]
+        _, xq, dxT = acts[(M, K)]
+        _lib.check(lib.axq8_linear_q8act_s(ws[i].c, C.c_void_p(xq.data_ptr()),
+                                           C.c_void_p(dxT.data_ptr()), M, None,
+                                           C.c_void_p(ys[(M, N)].data_ptr()), s_ptr))
+
+    K_steps, W_steps = args.steps, args.warmup
+    for _ in range(W_steps):
+        for M, i in cases:
+            product(M, i)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        with torch.cuda.graph(graph, stream=stream):
+            for M, i in cases:
+                product(M, i)
+    graph.replay()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device_uuid(dev)).start()
+    time.sleep(0.15)
+    d.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(K_steps):
+        graph.replay()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    d.barrier()
+    clk = clocks.stop()
+    ms_max = d.max(e0.elapsed_time(e1))
+    value = d.world * K_steps * step_bytes / (ms_max / 1e3) / 1e9
+
+    # per-product device times (one event pair per product, same order)
+    per = []
+    with torch.cuda.stream(stream):
+        evs = [torch.cuda.Event(enable_timing=True) for _ in range(len(cases) + 1)]
+        for rep in range(3):
+            evs[0].record(stream)
+            for j, (M, i) in enumerate(cases):
+                product(M, i)
+                evs[j + 1].record(stream)
+            torch.cuda.synchronize()
+            per.append([evs[j].elapsed_time(evs[j + 1]) for j in range(len(cases))])
+    per_us = [min(r[j] for r in per) * 1e3 for j in range(len(cases))]
+    # dominant launch: the largest weight at M = 64
+    jd = cases.index((64, 2))
+    alg = skinny_bytes(*SKINNY_SHAPES[2], 64)
+    peaks, peak_kind = measured_peaks()
+    achieved = alg / (per_us[jd] / 1e6) / 1e9
+    roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
+                "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
+                "traffic": ncu_traffic(SKINNY_CONFIG["workload"]),
+                "kernel": "q8_mmq_kernel<8> [28672x4096] M=64", "kernel_us": round(per_us[jd], 2),
+                "algorithmic_bytes": alg, "peak_source": peak_kind,
+                "per_product_us": {f"M{M} [{SKINNY_SHAPES[i][0]}x{SKINNY_SHAPES[i][1]}]":
+                                   round(per_us[j], 2) for j, (M, i) in enumerate(cases)}}
+
+    # e2e: the public call (axq8_linear, fp32 activations, its own A8
+    # quantization and dispatch) with pinned host input and output per product
+    xh = {k: torch.empty(v[0].shape, dtype=torch.float32, pin_memory=True) for k, v in acts.items()}
+    for k, v in acts.items():
+        xh[k].copy_(v[0].cpu())
+    yh = {k: torch.empty(v.shape, dtype=torch.float32, pin_memory=True) for k, v in ys.items()}
+    xd = {k: torch.empty_like(v[0]) for k, v in acts.items()}
+    h2d = sum(M * SKINNY_SHAPES[i][1] * 4 for M, i in cases)
+    d2h = sum(M * SKINNY_SHAPES[i][0] * 4 for M, i in cases)
+
+    def e2e_step():
+        for M, i in cases:
+            N, K = SKINNY_SHAPES[i]
+            xd[(M, K)].copy_(xh[(M, K)], non_blocking=True)
+            _lib.check(lib.axq8_linear(ws[i].c, C.c_void_p(xd[(M, K)].data_ptr()), M,
+                                       C.c_void_p(ys[(M, N)].data_ptr()), _lib.AXQ8_ACT_Q8, s_ptr))
+            yh[(M, N)].copy_(ys[(M, N)], non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for _ in range(W_steps):
+            e2e_step()
+        torch.cuda.synchronize()
+        d.barrier()
+        e0.record(stream)
+        n_e2e = min(K_steps, 50)
+        for _ in range(n_e2e):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize()
+    e2e_ms = d.max(e0.elapsed_time(e1))
+    e2e_val = d.world * n_e2e * step_bytes / (e2e_ms / 1e3) / 1e9
+    return {
+        "metric": SKINNY_METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": d.world,
+        "steps": K_steps, "warmup": W_steps, "ms_per_step": round(ms_max / K_steps, 5),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int8 x int8 -> int32 -> fp32 (mma.sync m16n8k32)",
+        "data": "synthetic (device-generated Q8_0 weights N(0,0.02); x N(0,1))",
+        "config": dict(SKINNY_CONFIG, act="q8 (pre-quantized, transposed scales)",
+                       l2_policy="221 MB of weights per pass, each weight reused only after "
+                                 "the other three (> L2)",
+                       parallelism=f"replicas x{d.world}"),
+        "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "steps": n_e2e,
+                "path": "axq8_linear (C ABI, A8, width dispatch) + pinned H2D/D2H per product"},
+        "roofline": roofline,
+        "gpu_launches": K_steps * len(cases),
+        "clocks": clk,
+        "device_status": ops.status(),
+    }
+
+
+def skinny_reference(args, rows: int) -> dict:
+    """The reference's linear at a decode width: load_tensor + linear_from_gguf
+    on one [4096 x 4096] Q8_0 weight at M = `rows`, host cores, as GB/s of the
+    same algorithmic bytes."""
+    import numpy as np
+    from axion_b200.gguf import Q8_0, GGUFWriter
+    from oracle.oracle import Oracle, RefLib
+    o, r = Oracle(), RefLib()
+    tmp = Path(tempfile.mkdtemp()) / "skinny.gguf"
+    gw = GGUFWriter()
+    gw.add_tensor("blk.0.attn_output.weight", o.synth_q8_0(L3_SEED + 1, 4096, 4096), (4096, 4096), Q8_0)
+    gw.write(tmp)
+    x = np.random.default_rng(0).normal(0, 1, (rows, 4096)).astype(np.float32)
+    r.time_linear(tmp, "blk.0.attn_output.weight", x[:1], 4096, 1)
+    sec, _ = r.time_linear(tmp, "blk.0.attn_output.weight", x, 4096, 1)
+    tmp.unlink()
+    val = skinny_bytes(4096, 4096, rows) / sec / 1e9
+    return {"value": round(val, 4), "unit": "GB/s", "cores": host_cores(), "kind": "reference",
+            "sample": f"GGUFLoader::load_tensor + linear_from_gguf, [4096x4096] Q8_0, M={rows}, "
+                      f"OpenMP threads={host_cores()}",
+            "seconds": round(sec, 3), "steps": 1}
+
+
+# ---------------------------------------------------------------------------
 # Prefill GEMM sweep (BASELINE config 3): Llama-2-7B linear shapes on the
 # tensor-core path
 # ---------------------------------------------------------------------------
@@ -851,6 +1035,7 @@ WORKLOADS = {
              200000, 300),
     "prefill": (run_prefill_axion, prefill_reference, PREFILL_METRIC, PREFILL_CONFIG, 16, 64),
     "llama3": (run_llama3_axion, llama3_reference, L3_METRIC, L3_CONFIG, L3_NEW, 16),
+    "skinny": (run_skinny_axion, skinny_reference, SKINNY_METRIC, SKINNY_CONFIG, 20, 16),
 }
 
 
