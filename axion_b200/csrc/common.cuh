@@ -117,6 +117,11 @@ __device__ inline void cp_async16_zfill(void* smem_dst, const void* gmem_src, bo
                  "l"(gmem_src), "r"(valid ? 16 : 0)
                  : "memory");
 }
+// 8 bytes (both addresses 8-byte aligned), through L1.
+__device__ inline void cp_async8(void* smem_dst, const void* gmem_src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(smem_u32(smem_dst)), "l"(gmem_src)
+                 : "memory");
+}
 __device__ inline void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 __device__ inline void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 // Wait until at most N of this thread's committed cp.async groups are pending.

@@ -232,9 +232,21 @@ MmqPlan mmq_plan(DeviceState* ds, int64_t N, int64_t K, int64_t M) {
 }
 template <int MT8>
 int mmq_launch(const MmqArgs& a, dim3 grid, cudaStream_t s) {
+    constexpr int smem = MmqSmem<MT8>::BYTES;
+    static bool configured[kMaxDevices] = {};
+    int dev = 0;
+    AXQ8_CUDA_TRY(cudaGetDevice(&dev), "q8_mmq device");
+    if (dev < 0 || dev >= kMaxDevices) return fail(AXQ8_ERR_INVALID, "skinny linear: device id");
+    if (!configured[dev]) {   // once per device: idempotent, a repeat is harmless
+        AXQ8_CUDA_TRY(cudaFuncSetAttribute(q8_mmq_kernel<MT8>,
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+                      "q8_mmq shared memory attribute");
+        configured[dev] = true;
+    }
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = dim3(kMmqWarps * 32);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = s;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

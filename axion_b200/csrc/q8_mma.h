@@ -18,20 +18,18 @@ constexpr int kMmaMinM = 32;
 // N >= 128, K a multiple of 128.
 bool mma_eligible(const axq8_weight_t* w, int64_t M);
 
-// Widths up to which the skinny product is preferred for every shape, and
-// the row count up to which it is preferred from there to kMmqMaxM rows (the
-// tcgen05 product's fixed costs dominate small weights; measured on B200 at
-// 64 rows: skinny 8.7-16 us vs 14-34 us for N <= 4096, even at N = 6144-7168,
-// tcgen05 ahead from N = 14336).
+// The skinny product is preferred up to kMmqMaxM rows for every shape: with
+// its weight tiles streamed through a shared-memory ring it matches or beats
+// the tcgen05 product there (measured on B200, M = 32..64, Llama-3-8B shapes
+// and their tensor-parallel slices: e.g. [128256x4096] 307 vs 336 us and
+// [28672x4096] 98 vs 158 us at M = 48, [768x4096] 16 vs 37 us at M = 64).
 constexpr int kMmqMaxM = 64;
-constexpr int kMmqPreferM = 32;
-constexpr int64_t kMmqPreferN = 8192;
 inline bool skinny_preferred(int64_t N, int64_t M) {
-    return M <= kMmqPreferM || (M <= kMmqMaxM && N <= kMmqPreferN);
+    (void)N;
+    return M <= kMmqMaxM;
 }
 
-// Whether axq8_linear takes the skinny product for w at M rows: 8 < M <= 64
-// where skinny_preferred holds or the tcgen05 product does not tile the shape.
+// Whether axq8_linear takes the skinny product for w at M rows: 8 < M <= 64.
 bool skinny_eligible(const axq8_weight_t* w, int64_t M);
 
 // Caller-owned split-K scratch (partials and per-tile counters, the counters

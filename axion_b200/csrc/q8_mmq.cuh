@@ -16,19 +16,23 @@
 // lane (g, t) takes the 8 contiguous bytes 8t..8t+7 of its rows' block for
 // the fragment slots of k 4t..4t+3 and 16+4t..16+4t+3, in the weight (rows g,
 // g+8) and the activation (row g of each 8-row tile) alike: every fragment is
-// one 8-byte load (global memory for the weights, shared for the activation).
+// one 8-byte load from shared memory.
 //
 // CTA: 8 warps x 16 weight rows = 128 rows over one range of K (blockIdx.y
-// splits K when the row tiles are few).  The activation rows and scales of
-// each 4-block chunk are staged once per CTA in shared memory with cp.async
-// (double buffered; 16-byte chunks XOR-swizzled by row so the 8-byte fragment
-// reads are conflict-free; rows past M and bytes past K zero-filled) and shared
-// by the 8 warps; each warp's weight fragments come straight from global
-// memory one chunk ahead.  The K splits of a row tile (blockIdx.y, at most 8)
-// run as one thread-block cluster: each CTA leaves its fp32 partial tile in
-// shared memory and, after a cluster barrier, every CTA adds one slice of the
-// tile over the cluster's partials in split order (distributed shared memory),
-// so the combine needs no global workspace and stays deterministic.
+// splits K when the row tiles are few).  Each 4-block chunk of K — the CTA's
+// 128 weight rows (16 KB, 16-byte pieces XOR-swizzled by row, kSwz, so the
+// 8-byte fragment reads are conflict-free), their block scales, the activation rows
+// (swizzled alike, zero-filled past M and K) and their scales — goes through a
+// ring of shared-memory stages (MmqSmem) with cp.async, several chunks in
+// flight: a weight stream needs about 44 KB in flight per SM to cover the HBM
+// latency, and one chunk ahead in registers left the warps waiting on it.
+// The first stages' weights are requested before the dependency wait
+// (programmatic dependent launch), the activations after it.  The K splits of
+// a row tile (blockIdx.y, at most 8) run as one thread-block cluster: each CTA
+// leaves its fp32 partial tile in shared memory (over the stages) and, after a
+// cluster barrier, every CTA adds one slice of the tile over the cluster's
+// partials in split order (distributed shared memory), so the combine needs
+// no global workspace and stays deterministic.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -46,17 +50,32 @@ constexpr int kMmqRows = 16 * kMmqWarps;   // weight rows per CTA
 constexpr int kMmqChunkKb = 4;             // 32-blocks per staged chunk (128 bytes of K)
 constexpr int kMmqMaxSplits = 8;           // cluster size limit (portable)
 
-// Shared memory of one CTA: the double-buffered activation chunk and scales
-// during the main loop, then (split launches) the fp32 partial tile [MR][kMmqTilePitch].
-constexpr int kMmqTilePitch = kMmqRows + 4;   // conflict-free fragment stores
+constexpr int kMmqTilePitch = kMmqRows + 4;   // fp32 partial tile row: conflict-free stores
+
+// Shared memory of one CTA: MmqSmem<MT8>::STAGES stages (2..6, about 104 KB) of
+//   W  [128 rows][128 B]  weight pieces (swizzled)      16 KB
+//   WS [128 rows][8 B]    their 4 fp16 block scales      1 KB
+//   X  [MR rows][128 B]   activation pieces (swizzled)
+//   DX [4 blocks][MR]     activation scales
+// then, for split launches, the fp32 partial tile [MR][kMmqTilePitch] over them.
 template <int MT8>
 struct MmqSmem {
     static constexpr int MR = 8 * MT8;
-    static constexpr int XS = 2 * MR * kMmqChunkKb * 32;
-    static constexpr int DXS = 2 * kMmqChunkKb * MR * 4;
+    static constexpr int W = 0;
+    static constexpr int WS = kMmqRows * kMmqChunkKb * 32;
+    static constexpr int X = WS + kMmqRows * 8;
+    static constexpr int DX = X + MR * kMmqChunkKb * 32;
+    static constexpr int STAGE = DX + kMmqChunkKb * MR * 4;
+    static constexpr int STAGES = 106496 / STAGE > 6 ? 6 : (106496 / STAGE < 2 ? 2 : 106496 / STAGE);
     static constexpr int TILE = MR * kMmqTilePitch * 4;
-    static constexpr int BYTES = XS + DXS > TILE ? XS + DXS : TILE;
+    static constexpr int BYTES = STAGES * STAGE > TILE ? STAGES * STAGE : TILE;
 };
+
+// Swizzle of a staged 128-byte row: its 16-byte piece p is stored at piece
+// p ^ kSwz(row).  A fragment read by a half-warp (4 rows g, 4 lanes t, each
+// lane 8 bytes at 32*k4 + 8t of its row) then touches 16 distinct 8-byte slots
+// of the 128-byte bank window: 32*(k4 ^ (g & 3)) + 8t.
+__device__ __forceinline__ int kSwz(int row) { return (row & 3) << 1; }
 
 struct MmqArgs {
     const uint8_t* rows;     // repacked Q8R rows
@@ -80,106 +99,104 @@ __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a, uint32_t
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "r"(c));
 }
 
-__device__ __forceinline__ uint2 ldg_nc8(const void* p) {
-    uint2 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v2.u32 {%0, %1}, [%2];"
-                 : "=r"(v.x), "=r"(v.y)
-                 : "l"(p));
-    return v;
-}
-
-// One chunk's weight fragments of a lane: rows g and g+8 of its warp's 16,
-// bytes 8t..8t+7 of each of the 4 blocks, and the 4 block scales of both rows.
-struct MmqWeights {
-    uint2 a[kMmqChunkKb][2];
-    uint2 s[2];
-};
-
-// Launched with cluster dimensions (1, gridDim.y, 1) when gridDim.y > 1.
+// Launched with cluster dimensions (1, gridDim.y, 1) when gridDim.y > 1, and
+// MmqSmem<MT8>::BYTES of dynamic shared memory.
 template <int MT8>   // 8-row activation tiles (M <= 8 * MT8)
 __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs a) {
     constexpr uint32_t kMagicBitsI = 0x4B400000u;   // 1.5 * 2^23 as fp32
     constexpr float kMagicF = 12582912.0f;
     using SM = MmqSmem<MT8>;
     constexpr int MR = SM::MR;                      // staged activation rows
-    __shared__ __align__(16) uint8_t smem[SM::BYTES];
-    auto xs = reinterpret_cast<uint8_t(*)[MR][kMmqChunkKb * 32]>(smem);
-    auto dxs = reinterpret_cast<float(*)[kMmqChunkKb][MR]>(smem + SM::XS);
+    constexpr int NST = SM::STAGES;
+    extern __shared__ __align__(128) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int g = lane >> 2, t = lane & 3;
-    const int n0 = blockIdx.x * kMmqRows + warp * 16;
+    const int nbase = blockIdx.x * kMmqRows;
+    const int n0 = nbase + warp * 16;
     const int nkb = a.K / 32;
     const int nch = (nkb + kMmqChunkKb - 1) / kMmqChunkKb;
     const int ch0 = blockIdx.y * a.chunks_per_split, ch1 = min(nch, ch0 + a.chunks_per_split);
-    const int ra = min(n0 + g, a.N - 1), rb = min(n0 + g + 8, a.N - 1);
-    const uint8_t* wa = a.rows + (int64_t)ra * a.row_stride;
-    const uint8_t* wb = a.rows + (int64_t)rb * a.row_stride;
-    auto load_w = [&](int ch, MmqWeights& W) {
-#pragma unroll
-        for (int k4 = 0; k4 < kMmqChunkKb; k4++) {
-            const int kb = ch * kMmqChunkKb + k4;
-            if (kb < nkb) {
-                W.a[k4][0] = ldg_nc8(wa + kb * 32 + 8 * t);
-                W.a[k4][1] = ldg_nc8(wb + kb * 32 + 8 * t);
-            } else {
-                W.a[k4][0] = W.a[k4][1] = make_uint2(0, 0);
-            }
+    // weights (and their scales) of chunk ch into stage st
+    auto issue_w = [&](int ch, int st) {
+        uint8_t* W = smem + st * SM::STAGE + SM::W;
+        for (int i = threadIdx.x; i < kMmqRows * 8; i += blockDim.x) {
+            const int r = i >> 3, pc = i & 7;
+            const int64_t n = min(nbase + r, a.N - 1);
+            const int kbyte = ch * kMmqChunkKb * 32 + pc * 16;
+            const bool ok = kbyte < a.K;
+            cp_async16_zfill(W + r * 128 + ((pc ^ kSwz(r)) << 4),
+                             a.rows + n * a.row_stride + (ok ? kbyte : 0), ok);
         }
         // 4 fp16 scales per row; the row's scale area is padded to 16 bytes
-        W.s[0] = ldg_nc8(wa + a.K + ch * kMmqChunkKb * 2);
-        W.s[1] = ldg_nc8(wb + a.K + ch * kMmqChunkKb * 2);
+        uint8_t* WS = smem + st * SM::STAGE + SM::WS;
+        for (int r = threadIdx.x; r < kMmqRows; r += blockDim.x) {
+            const int64_t n = min(nbase + r, a.N - 1);
+            cp_async8(WS + r * 8, a.rows + n * a.row_stride + a.K + ch * kMmqChunkKb * 2);
+        }
     };
-    auto stage_x = [&](int ch, int buf) {
-        // activation quants: MR rows x 8 chunks of 16 bytes, swizzled by row
+    // activation rows and scales of chunk ch into stage st
+    auto issue_x = [&](int ch, int st) {
+        uint8_t* X = smem + st * SM::STAGE + SM::X;
+        float* DX = reinterpret_cast<float*>(smem + st * SM::STAGE + SM::DX);
         for (int i = threadIdx.x; i < MR * 8; i += blockDim.x) {
             const int r = i >> 3, c = i & 7;
             const int64_t k = (int64_t)ch * kMmqChunkKb * 32 + c * 16;
             const bool ok = r < a.M && k < a.K;
-            cp_async16_zfill(&xs[buf][r][(c ^ (r & 7)) * 16], a.xq + (ok ? (int64_t)r * a.K + k : 0), ok);
+            cp_async16_zfill(X + r * 128 + ((c ^ kSwz(r)) << 4), a.xq + (ok ? (int64_t)r * a.K + k : 0), ok);
         }
         // scales: 4 blocks x MR rows, 16 bytes = 4 rows per copy
         for (int i = threadIdx.x; i < kMmqChunkKb * MR / 4; i += blockDim.x) {
             const int k4 = i / (MR / 4), r4 = (i % (MR / 4)) * 4;
             const int kb = ch * kMmqChunkKb + k4;
             const bool ok = kb < nkb && r4 < a.Mp;
-            cp_async16_zfill(&dxs[buf][k4][r4], a.dxT + (ok ? (int64_t)kb * a.Mp + r4 : 0), ok);
+            cp_async16_zfill(DX + k4 * MR + r4, a.dxT + (ok ? (int64_t)kb * a.Mp + r4 : 0), ok);
         }
     };
     float2 acc[MT8][2];   // [j][0]: row g, columns 8j + 2t (+1); [j][1]: row g + 8
 #pragma unroll
     for (int j = 0; j < MT8; j++) acc[j][0] = acc[j][1] = make_float2(0.0f, 0.0f);
-    MmqWeights Wc, Wn;
-    if (ch0 < ch1) load_w(ch0, Wc);          // weights are static: before the wait
+    // weights are static: the first NST - 1 chunks' weights before the wait
+    for (int s = 0; s < NST - 1; s++)
+        if (ch0 + s < ch1) issue_w(ch0 + s, s);
     pdl_launch_dependents();
     pdl_wait();
-    if (ch0 < ch1) stage_x(ch0, 0);
-    cp_async_commit();
+    for (int s = 0; s < NST - 1; s++) {
+        if (ch0 + s < ch1) issue_x(ch0 + s, s);
+        cp_async_commit();   // group s (group 0 also holds the early weights)
+    }
+    const int ra = warp * 16 + g, rb = ra + 8;   // this lane's rows in the tile; both & 3 == g & 3
     for (int ch = ch0; ch < ch1; ch++) {
-        const int buf = (ch - ch0) & 1;
-        if (ch + 1 < ch1) {
-            load_w(ch + 1, Wn);
-            stage_x(ch + 1, buf ^ 1);
-            cp_async_commit();
-            cp_async_wait_group<1>();
-        } else {
-            cp_async_wait_group<0>();
+        const int i = ch - ch0;
+        cp_async_wait_group<NST - 2>();   // chunk ch has landed
+        __syncthreads();                  // ... for every thread; stage (i - 1) % NST is free
+        if (ch + NST - 1 < ch1) {
+            issue_w(ch + NST - 1, (i + NST - 1) % NST);
+            issue_x(ch + NST - 1, (i + NST - 1) % NST);
         }
-        __syncthreads();
+        cp_async_commit();
+        const uint8_t* st = smem + (i % NST) * SM::STAGE;
+        const uint8_t* W = st + SM::W;
+        const uint8_t* X = st + SM::X;
+        const float* DX = reinterpret_cast<const float*>(st + SM::DX);
+        const uint2 sa = *reinterpret_cast<const uint2*>(st + SM::WS + ra * 8);
+        const uint2 sb = *reinterpret_cast<const uint2*>(st + SM::WS + rb * 8);
 #pragma unroll
         for (int k4 = 0; k4 < kMmqChunkKb; k4++) {
-            const uint32_t af[4] = {Wc.a[k4][0].x, Wc.a[k4][1].x, Wc.a[k4][0].y, Wc.a[k4][1].y};
-            const uint32_t swa = (k4 < 2 ? Wc.s[0].x : Wc.s[0].y) >> ((k4 & 1) * 16);
-            const uint32_t swb = (k4 < 2 ? Wc.s[1].x : Wc.s[1].y) >> ((k4 & 1) * 16);
+            // the 16-byte piece holding bytes 8t..8t+7 of block k4, and the half of it
+            const int c16 = (k4 * 32 + 8 * t) >> 4, c8 = (8 * t) & 15;
+            const uint2 A0 = *reinterpret_cast<const uint2*>(W + ra * 128 + ((c16 ^ kSwz(g)) << 4) + c8);
+            const uint2 A1 = *reinterpret_cast<const uint2*>(W + rb * 128 + ((c16 ^ kSwz(g)) << 4) + c8);
+            const uint32_t af[4] = {A0.x, A1.x, A0.y, A1.y};
+            const uint32_t swa = (k4 < 2 ? sa.x : sa.y) >> ((k4 & 1) * 16);
+            const uint32_t swb = (k4 < 2 ? sb.x : sb.y) >> ((k4 & 1) * 16);
             const float dwa = __half2float(__ushort_as_half((unsigned short)(swa & 0xFFFFu)));
             const float dwb = __half2float(__ushort_as_half((unsigned short)(swb & 0xFFFFu)));
             const float nca = -kMagicF * dwa, ncb = -kMagicF * dwb;
-            // the chunk's 16-byte piece holding bytes 8t..8t+7 of block k4
-            const int c16 = (k4 * 32 + 8 * t) >> 4, c8 = (8 * t) & 15;
 #pragma unroll
             for (int j = 0; j < MT8; j++) {
                 const int r = 8 * j + g;
-                const uint2 B = *reinterpret_cast<const uint2*>(&xs[buf][r][((c16 ^ (r & 7)) << 4) + c8]);
-                const float2 dxv = *reinterpret_cast<const float2*>(&dxs[buf][k4][8 * j + 2 * t]);
+                const uint2 B = *reinterpret_cast<const uint2*>(X + r * 128 + ((c16 ^ kSwz(r)) << 4) + c8);
+                const float2 dxv = *reinterpret_cast<const float2*>(DX + k4 * MR + 8 * j + 2 * t);
                 int d[4];
                 mma_s8_16832(d, af, B.x, B.y, (int)kMagicBitsI);
                 const float2 ta = ffma2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])),
@@ -190,10 +207,8 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
                 acc[j][1] = ffma2(tb, dxv, acc[j][1]);
             }
         }
-        Wc = Wn;
-        __syncthreads();   // buffer `buf` is free for chunk ch + 2
     }
-    if (ch0 >= ch1) cp_async_wait_all();
+    cp_async_wait_all();   // nothing of this CTA still lands in the stages
     // outputs: rows n0 + g (+8), columns 8j + 2t (+1)
     const int splits = gridDim.y;
     if (splits == 1) {

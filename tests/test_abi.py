@@ -98,14 +98,12 @@ def test_tensor_core_entry_points_validate_shapes():
     w.K, w.row_stride = 256, lib.axq8_row_stride(256)
     assert lib.axq8_linear_path(ctypes.byref(w), 1, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_GEMV
     assert lib.axq8_linear_path(ctypes.byref(w), 32, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_SKINNY
-    # 32 < M <= 64: skinny for N <= 8192 rows, the tcgen05 product beyond
+    # up to 64 rows the skinny product for every shape, the tcgen05 product beyond
     assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_SKINNY
     assert lib.axq8_linear_path(ctypes.byref(w), 65, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_TENSOR_CORE
-    w.N = 8192
+    w.N = 131072
     assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_SKINNY
-    w.N = 8320
-    assert lib.axq8_linear_path(ctypes.byref(w), 33, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_TENSOR_CORE
-    assert lib.axq8_linear_path(ctypes.byref(w), 32, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_SKINNY
+    assert lib.axq8_linear_path(ctypes.byref(w), 65, _lib.AXQ8_ACT_Q8) == _lib.AXQ8_PATH_TENSOR_CORE
     w.N = 256
     rc = lib.axq8_linear_q8act_s(ctypes.byref(w), 4096, 4096, 65, None, 4096, None)
     assert rc == _lib.AXQ8_ERR_UNSUPPORTED and b"M <= 64" in lib.axq8_last_error()

@@ -84,7 +84,7 @@ def test_tensor_core_linear_vs_oracle(cuda, oracle, N, K, M):
     ops = _ops()
     blocks, x, w = _case(oracle, N, K, M, seed=7 * N + M)
     xt = torch.from_numpy(x).cuda()
-    assert ops.linear_path(w, M) == ("skinny" if M <= 32 or (M <= 64 and N <= 8192) else "tensor_core")
+    assert ops.linear_path(w, M) == ("skinny" if M <= 64 else "tensor_core")
     xq, dxT = ops.quantize_activations_t(xt)
     y = ops.linear_q8act_t(w, xq, dxT).cpu().numpy()      # the tcgen05 product at every M
     oq, od = oracle.quantize_act(x)
@@ -159,7 +159,7 @@ def test_dispatch_by_width(cuda, oracle):
     assert ops.linear_path(w, 8) == "gemv"
     assert ops.linear_path(w, 9) == "skinny"
     assert ops.linear_path(w, 32) == "skinny"
-    assert ops.linear_path(w, 64) == "skinny"          # N <= 8192
+    assert ops.linear_path(w, 64) == "skinny"
     assert ops.linear_path(w, 65) == "tensor_core"
     assert ops.linear_path(w, 64, "f32") == "gemv"
     _, _, w2 = _case(oracle, 64, 256, 1, seed=0)
