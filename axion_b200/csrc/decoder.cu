@@ -726,11 +726,18 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->rs_f = q8r_row_stride(c.ffn);
     m->max_blocks = (c.max_ctx + c.kv_block - 1) / c.kv_block;
     // split the context so that attention gives about four CTAs per SM at full
-    // length, with at least 2 pages per split and at most 32 splits (the
+    // length, down to one page per split (AXDEC_ATTN_MIN_PAGES overrides,
+    // tuning; measured at batch 1, 384-token context: 1 page 1,202 tokens/s,
+    // 2 pages 1,166, 4 pages 998, one split 710), at most 32 splits (the
     // merge gives one lane to each split)
+    const int min_pages = [] {
+        const char* e = getenv("AXDEC_ATTN_MIN_PAGES");
+        const int v = e ? atoi(e) : 1;
+        return v >= 1 && v <= 4096 ? v : 1;
+    }();
     const int target = (4 * ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
                        (c.n_kv_heads * c.max_batch);
-    m->nsplit = std::max(1, std::min(std::min(target, (m->max_blocks + 1) / 2), 32));
+    m->nsplit = std::max(1, std::min(std::min(target, (m->max_blocks + min_pages - 1) / min_pages), 32));
     m->bps = (m->max_blocks + m->nsplit - 1) / m->nsplit;
     m->nsplit = (m->max_blocks + m->bps - 1) / m->bps;
     int rc = AXQ8_OK;
