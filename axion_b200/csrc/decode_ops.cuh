@@ -772,9 +772,10 @@ __global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key,
 }
 
 // ---- SiLU(gate) * up (+ A8 quantization) -------------------------------------------
-// gu row = [gate (F) | up (F)].  a = (g / (1 + e^-g)) * u, rounded per op as
-// silu.cpp and elementwise.cpp do.  8 consecutive elements per thread (4
-// threads per 32-block); F % 32 == 0.
+// gu row = (gate_0, up_0, gate_1, up_1, ...): the product of the gate|up weight
+// stored with gate row j and up row j interleaved.  a = (g / (1 + e^-g)) * u,
+// rounded per op as silu.cpp and elementwise.cpp do.  8 consecutive outputs
+// per thread (4 threads per 32-block); F % 32 == 0.
 template <bool Q8>
 __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
                                 float* __restrict__ out, int8_t* __restrict__ xq,
@@ -788,8 +789,14 @@ __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
     const int m = valid ? (int)(j / nu) : 0, c = valid ? (int)(j % nu) : 0;
     float g[8], u[8], a[8];
     if (valid) {
-        load8(gu + (int64_t)m * 2 * F + 8 * c, g);
-        load8(gu + (int64_t)m * 2 * F + F + 8 * c, u);
+        float p[16];
+        load8(gu + (int64_t)m * 2 * F + 16 * c, *reinterpret_cast<float(*)[8]>(p));
+        load8(gu + (int64_t)m * 2 * F + 16 * c + 8, *reinterpret_cast<float(*)[8]>(p + 8));
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            g[e] = p[2 * e];
+            u[e] = p[2 * e + 1];
+        }
     } else {
 #pragma unroll
         for (int e = 0; e < 8; e++) g[e] = u[e] = 0.0f;

@@ -8,13 +8,14 @@
 //   GEMV qkv   [prologue rmsnorm->Q8, epilogue NEOX RoPE + KV page append]
 //   attention  [split-K flash decode, last CTA merges splits -> Q8]
 //   GEMV o     [+ residual, in place]
-//   GEMV gu    [prologue rmsnorm->Q8]
-//   GEMV down  [prologue silu(gate)*up->Q8, + residual]
+//   GEMV gu    [prologue rmsnorm->Q8, epilogue silu(gate)*up]
+//   GEMV down  [prologue Q8, + residual]
 // plus embed at the start and GEMV lm_head [prologue rmsnorm->Q8, epilogue
 // argmax + state advance] at the end.  A32 mode and wide batches keep
 // RMSNorm and SiLU*up as producer kernels.  Q, K and V share one stacked
 // weight (the rows of Q and K permuted per head to (j, j + hd/2) pairs for
-// the RoPE epilogue), and so do gate and up.  All kernels are launched
+// the RoPE epilogue), and so do gate and up (rows interleaved, gate_j then
+// up_j, so one GEMV row pair yields one silu(gate_j)*up_j).  All kernels are launched
 // with programmatic dependent launch and the whole step is captured once in a
 // CUDA graph per batch size; the control state (positions, input tokens, fed
 // tokens) lives in device memory so the same graph serves every step.
@@ -48,7 +49,7 @@ namespace {
 struct Layer {
     uint8_t* qkv = nullptr;    // [Nq + 2 Nkv, H] Q8R
     uint8_t* o = nullptr;      // [H, Nq]
-    uint8_t* gu = nullptr;     // [2F, H]
+    uint8_t* gu = nullptr;     // [2F, H], rows gate_0, up_0, gate_1, up_1, ...
     uint8_t* down = nullptr;   // [H, F]
     float* attn_norm = nullptr;
     float* ffn_norm = nullptr;
@@ -85,7 +86,7 @@ struct axdec_model {
     float* dx = nullptr;          // [M, maxK/32]
     float* x32 = nullptr;         // [M, maxK] (A32 mode)
     float* qkv = nullptr;         // [M, Nqkv]
-    float* gu = nullptr;          // [M, 2F]
+    float* gu = nullptr;          // [M, 2F] interleaved gate/up, or [M, F] silu*up (fused GEMV)
     float* part = nullptr;        // attention partials
     float* logits = nullptr;      // [M, V]
     float2* rope = nullptr;       // [max_ctx, hd/2]
@@ -148,6 +149,7 @@ struct Dest {
     float* f32 = nullptr;   // norm weight destination
     int64_t n = 0;
     bool rope_perm = false; // attn_q / attn_k: rows permuted for the RoPE epilogue
+    int row_step = 1;       // destination row of source row i: row0 + i * row_step
     // this rank's slice of the whole [src_N, src_K] tensor (rows src_row0..,
     // columns src_col0..); the whole tensor when not split
     int64_t src_row0 = 0, src_col0 = 0, src_N = 0, src_K = 0;
@@ -193,8 +195,9 @@ int resolve(axdec_model* m, const char* name, Dest* d) {
         case 2: rows_slice(Ly.qkv, m->Nq, m->Nkv, Nkvf, (int64_t)r * m->Nkv); d->rope_perm = true; return 0;
         case 3: rows_slice(Ly.qkv, m->Nq + m->Nkv, m->Nkv, Nkvf, (int64_t)r * m->Nkv); return 0;
         case 4: cols_slice(Ly.o, m->Nq, Nqf, (int64_t)r * m->Nq); return 0;
-        case 6: rows_slice(Ly.gu, 0, F, Ff, (int64_t)r * F); return 0;
-        case 7: rows_slice(Ly.gu, F, F, Ff, (int64_t)r * F); return 0;
+        // gate and up interleaved: gate row j -> row 2j, up row j -> row 2j + 1
+        case 6: rows_slice(Ly.gu, 0, F, Ff, (int64_t)r * F); d->row_step = 2; return 0;
+        case 7: rows_slice(Ly.gu, 1, F, Ff, (int64_t)r * F); d->row_step = 2; return 0;
         case 8: cols_slice(Ly.down, F, Ff, (int64_t)r * F); return 0;
         default: return fail(AXQ8_ERR_INVALID, "axdec: unknown tensor '%s'", name);
     }
@@ -236,13 +239,27 @@ __global__ void rope_permute_rows_kernel(const uint8_t* __restrict__ src, uint8_
     }
 }
 
-// Write repacked rows (device, `tmp`) into the destination, permuting Q/K rows.
+// Row i of src to row i * step of dst (rows of rs bytes, rs % 16 == 0).
+__global__ void scatter_rows_kernel(const uint8_t* __restrict__ src, uint8_t* __restrict__ dst,
+                                    int64_t nrows, int step, int64_t rs) {
+    for (int64_t r = blockIdx.x; r < nrows; r += gridDim.x) {
+        const uint4* s4 = reinterpret_cast<const uint4*>(src + r * rs);
+        uint4* d4 = reinterpret_cast<uint4*>(dst + r * step * rs);
+        for (int64_t i = threadIdx.x; i < rs / 16; i += blockDim.x) d4[i] = s4[i];
+    }
+}
+
+// Write repacked rows (device, `tmp`) into the destination, permuting Q/K rows
+// and interleaving gate/up rows.
 int place_rows(axdec_model* m, const Dest& d, const uint8_t* tmp) {
     const int64_t rs = q8r_row_stride(d.K);
     uint8_t* dst = d.rows + d.row0 * rs;
     if (d.rope_perm) {
         rope_permute_rows_kernel<<<256, 128>>>(tmp, dst, d.N, m->c.head_dim, rs);
         AXQ8_CUDA_TRY(cudaGetLastError(), "rope_permute_rows launch");
+    } else if (d.row_step != 1) {
+        scatter_rows_kernel<<<256, 128>>>(tmp, dst, d.N, d.row_step, rs);
+        AXQ8_CUDA_TRY(cudaGetLastError(), "scatter_rows launch");
     } else {
         AXQ8_CUDA_TRY(cudaMemcpy(dst, tmp, (size_t)d.N * rs, cudaMemcpyDeviceToDevice), "place rows");
     }
@@ -470,7 +487,7 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
     const bool a32 = c.act_mode == AXQ8_ACT_F32;
     // fused producers: A8 and the activations of M rows fit in shared memory
     const bool fuse = !a32 && gemv_fused_prologue_fits(PRO_RMS, M, H) &&
-                      gemv_fused_prologue_fits(PRO_SILU, M, F);
+                      gemv_fused_prologue_fits(PRO_QNT, M, F);
     const int plain = a32 ? PRO_F32 : PRO_Q8;
     DeviceState* ds = m->ds;
     int rc;
@@ -516,12 +533,13 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
                               : gemv_launch_mt<PRO_Q8, EPI_STORE, float>(ds, a, s);
         if (rc) return rc;
         if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
-        // gate | up
+        // gate | up (fused: + SiLU*up in the epilogue, rows are (gate_j, up_j) pairs)
         a = gemv_args(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu);
         if (fuse) {
             a.src = m->h;
             a.norm_w = Ly.ffn_norm;
-            rc = gemv_launch_mt<PRO_RMS, EPI_STORE, float>(ds, a, s);
+            a.ldy = F;
+            rc = gemv_launch_mt<PRO_RMS, EPI_SILU, float>(ds, a, s);
         } else {
             if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s))) return rc;
             rc = a32 ? gemv_launch_mt<PRO_F32, EPI_STORE, float>(ds, a, s)
@@ -531,8 +549,8 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
         // down + residual
         a = gemv_args(m, Ly.down, H, F, M, resid, m->h);
         if (fuse) {
-            a.src = m->gu;
-            rc = gemv_launch_mt<PRO_SILU, EPI_STORE, float>(ds, a, s);
+            a.src = m->gu;   // SiLU*up [M][F], quantized in the prologue
+            rc = gemv_launch_mt<PRO_QNT, EPI_STORE, float>(ds, a, s);
         } else {
             if (a32) {
                 AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<false>, silu_grid(M, F), dim3(kSiluThreads), 0,
@@ -961,7 +979,7 @@ int axdec_init_random(axdec_model_t* m, uint64_t seed, float stdv) {
         }
         // this rank's slice of the tensor axq8_synth_q8_0(sd, src_N, src_K) generates
         const uint64_t sd = seed + (uint64_t)axdec_tensor_index(&c, n.c_str());
-        if (!d.rope_perm) {
+        if (!d.rope_perm && d.row_step == 1) {
             rc = synth_q8_0_slice(sd, d.N, d.K, d.src_row0, d.src_col0, d.src_K, 0.0f, stdv,
                                   d.rows + d.row0 * q8r_row_stride(d.K), nullptr);
             if (rc) return rc;

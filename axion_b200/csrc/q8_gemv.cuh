@@ -27,13 +27,17 @@
 //   PRO_F32   fp32 x read from global memory (A32);
 //   PRO_RMS   RMSNorm of src[M,K] by norm_w, quantized to Q8 in shared memory
 //             (every CTA computes the same bytes; replaces a producer kernel);
-//   PRO_SILU  silu(gate)*up of src[M, 2K] quantized to Q8 in shared memory.
+//   PRO_QNT   fp32 src[M, K] quantized to Q8 in shared memory (the SiLU*up
+//             rows an EPI_SILU launch wrote).
 // Epilogues (EPI) consume the two sums of a row pair:
 //   EPI_STORE   y = residual + sum;
 //   EPI_ROPE_KV the rows of Q and K are stored permuted so that a pair is
 //               (dim j, dim j + hd/2) of one head: rotate (NEOX RoPE) and
 //               write q back in natural order / k into the KV pages; v rows
 //               go to the V pages (replaces rope_apply_row_at + append_row);
+//   EPI_SILU    the rows are (gate_j, up_j) pairs (the stacked gate|up weight
+//               stored interleaved): y[m, j] = silu(gate_j) * up_j, rounded per op
+//               as silu.cpp:53-61 and elementwise.cpp:55-63 do (ldy = N / 2);
 //   EPI_ARGMAX  store the logits and reduce the greedy argmax over the grid
 //               (packed atomicMax); the last CTA to finish advances the
 //               decode state (next input token, position, generated token).
@@ -51,8 +55,8 @@
 
 namespace axq8 {
 
-enum { PRO_Q8 = 0, PRO_F32 = 1, PRO_RMS = 2, PRO_SILU = 3 };
-enum { EPI_STORE = 0, EPI_ROPE_KV = 1, EPI_ARGMAX = 2 };
+enum { PRO_Q8 = 0, PRO_F32 = 1, PRO_RMS = 2, PRO_QNT = 3 };
+enum { EPI_STORE = 0, EPI_ROPE_KV = 1, EPI_ARGMAX = 2, EPI_SILU = 3 };
 
 struct GemvArgs {
     const uint8_t* rows;      // Q8R rows
@@ -66,8 +70,8 @@ struct GemvArgs {
     int64_t ldy;
     int* status;
     int act_smem;             // bytes of staged activation (0: read from global)
-    // PRO_RMS / PRO_SILU
-    const float* src;         // RMS: [M, K]; SILU: [M, 2K] = [gate | up]
+    // PRO_RMS / PRO_QNT
+    const float* src;         // RMS, QNT: [M, K]
     const float* norm_w;      // RMS weight [K]
     float eps;
     // EPI_ROPE_KV
@@ -285,6 +289,11 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, int m, int64_t n, bo
         }
         return;
     }
+    if (EPI == EPI_SILU) {   // rows n, n + 1 = gate_j, up_j with j = n / 2
+        const float act = __fmul_rn(__fdiv_rn(v0, __fadd_rn(1.0f, expf(-v0))), v1);
+        a.y[(int64_t)m * a.ldy + n / 2] = act;
+        return;
+    }
 #pragma unroll
     for (int r = 0; r < 2; r++) {
         if (r == 1 && !has_b) break;
@@ -365,30 +374,23 @@ __device__ __forceinline__ void prologue_rms(const GemvArgs& a, int8_t* act_q, f
     }
 }
 
-// PRO_SILU: act <- Q8(silu(gate) * up), a = (g / (1 + e^-g)) * u rounded per
-// op as silu.cpp:53-61 and elementwise.cpp:55-63 do.  stage: src [M][2K].
+// PRO_QNT: act <- Q8(src[m, :]).  stage: src [M][K].
 template <int NW>
-__device__ __forceinline__ void prologue_silu(const GemvArgs& a, int8_t* act_q, float* act_d,
-                                              float* stage) {
+__device__ __forceinline__ void prologue_qnt(const GemvArgs& a, int8_t* act_q, float* act_d,
+                                             float* stage) {
     const int K = (int)a.K, nb = K / QK, M = a.M;
     const int lane = threadIdx.x & 31;
     constexpr int T = NW * 32;
-    for (int i = threadIdx.x; i < M * 2 * K / 4; i += T) cp_async16(stage + 4 * i, a.src + 4 * i);
+    for (int i = threadIdx.x; i < M * K / 4; i += T) cp_async16(stage + 4 * i, a.src + 4 * i);
     cp_async_wait_all();
     __syncthreads();
     for (int m = 0; m < M; m++) {
-        const float4* g4 = reinterpret_cast<const float4*>(stage + (int64_t)m * 2 * K);
-        const float4* u4 = reinterpret_cast<const float4*>(stage + (int64_t)m * 2 * K + K);
-        for (int q0 = 0; q0 < K / 4; q0 += T) {
+        const float4* x4 = reinterpret_cast<const float4*>(stage + (int64_t)m * K);
+        for (int q0 = 0; q0 < K / 4; q0 += T) {      // uniform trip count: whole 8-lane groups
             const int q = q0 + threadIdx.x;
             if (q < K / 4) {
-                const float4 gv = g4[q], uv = u4[q];
-                const float gg[4] = {gv.x, gv.y, gv.z, gv.w};
-                const float uu[4] = {uv.x, uv.y, uv.z, uv.w};
-                float v[4];
-#pragma unroll
-                for (int j = 0; j < 4; j++)
-                    v[j] = __fmul_rn(__fdiv_rn(gg[j], __fadd_rn(1.0f, expf(-gg[j]))), uu[j]);
+                const float4 xv = x4[q];
+                const float v[4] = {xv.x, xv.y, xv.z, xv.w};
                 quant_quad(v, lane, act_q + m * K + 4 * q, act_d + m * nb + q / 8);
             }
         }
@@ -492,8 +494,8 @@ __global__ void __launch_bounds__(kGemvWarps * 32, kGemvCtasPerSm) q8_gemv_kerne
             prologue_rms<kGemvWarps>(a, act_q, act_d, part, stage);
             xq = act_q;
             dx = act_d;
-        } else if (PRO == PRO_SILU) {
-            prologue_silu<kGemvWarps>(a, act_q, act_d, stage);
+        } else if (PRO == PRO_QNT) {
+            prologue_qnt<kGemvWarps>(a, act_q, act_d, stage);
             xq = act_q;
             dx = act_d;
         }
@@ -587,11 +589,11 @@ inline int64_t gemv_act_bytes(int M, int64_t K) {
 // Bytes of the fused prologue's input staging area.
 inline int64_t gemv_stage_bytes(int pro, int M, int64_t K) {
     if (pro == PRO_RMS) return ((int64_t)M * K + K) * 4;
-    if (pro == PRO_SILU) return (int64_t)M * 2 * K * 4;
+    if (pro == PRO_QNT) return (int64_t)M * K * 4;
     return 0;
 }
 
-// Whether a fused prologue (PRO_RMS / PRO_SILU) fits for M rows of K.
+// Whether a fused prologue (PRO_RMS / PRO_QNT) fits for M rows of K.
 inline bool gemv_fused_prologue_fits(int pro, int M, int64_t K) {
     return M <= kGemvMaxMT && K <= kProMaxK && gemv_act_bytes(M, K) <= kGemvActSmemMax &&
            gemv_stage_bytes(pro, M, K) <= kProStageMax;
@@ -601,7 +603,7 @@ template <int MT, int PRO, int EPI, typename KV>
 inline int gemv_launch_t(DeviceState* ds, GemvArgs a, cudaStream_t stream) {
     if (a.K > (1 << 24) || (int64_t)a.M * a.K > (1ll << 31))
         return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: K or M*K too large");
-    if ((PRO == PRO_RMS || PRO == PRO_SILU) && (a.M > MT || a.K > kProMaxK))
+    if ((PRO == PRO_RMS || PRO == PRO_QNT) && (a.M > MT || a.K > kProMaxK))
         return fail(AXQ8_ERR_UNSUPPORTED, "q8 gemv: fused prologue with M=%d, K=%lld", a.M,
                     (long long)a.K);
     if (EPI == EPI_ARGMAX && a.M > kArgmaxMaxM)
