@@ -28,7 +28,7 @@ Workloads
          theta 5e5 (not given by the config; Llama-3's), batch 64, random
          2048-token prompts, then K (default 128) greedy steps; tensor parallel
          over the N GPUs of the run (strong scaling).  Every linear runs on the
-         skinny or the tcgen05 product at M = 64 (by shape).  Metric: decode
+         skinny product at M = 64.  Metric: decode
          tokens/s of the whole job; the reference arm is extrapolated from one
          linear.
   skinny the decode-width product (q8_mmq_kernel, mma.sync int8 with register
@@ -567,7 +567,7 @@ L3_METRIC = "Llama-3-8B-arch Q8_0 batched decode tokens/s (batch 64, 2048-token 
 L3_CONFIG = {"workload": "llama3_8b_arch_decode_b64_tp", "layers": 32, "hidden": 4096,
              "ffn": 14336, "heads": "32q/8kv x 128", "vocab": 128256, "rope_theta": 500000.0,
              "batch": L3_BATCH, "prompt": L3_PROMPT, "new_tokens": L3_NEW,
-             "kv": "paged fp16, block 16", "act": "q8 (A8W8, tcgen05 kind::i8 for M = 64)"}
+             "kv": "paged fp16, block 16", "act": "q8 (A8W8, skinny mma.sync int8 product at M = 64)"}
 
 
 def run_llama3_axion(args, d: Dist) -> dict:
@@ -621,7 +621,7 @@ def run_llama3_axion(args, d: Dist) -> dict:
     peaks, peak_kind = measured_peaks()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": None, "kernel": "decode step per rank (q8_mma_kernel dominant)",
+                "traffic": None, "kernel": "decode step per rank (q8_mmq_kernel dominant)",
                 "step_us": round(step_ms * 1e3, 1),
                 "algorithmic_bytes_per_step_per_rank": int(wbytes + kv_bytes),
                 "peak_source": peak_kind}

@@ -91,10 +91,10 @@ int axq8_quantize_act(const float* x, int64_t M, int64_t K, int8_t* xq, float* d
  * the quantized activations live in a per-device workspace that this
  * library allocates on first use and grows when a larger M*K arrives (the
  * only allocation on this path); calls on different streams of one device
- * must not overlap.  A8 with 8 < M <= 32 runs the skinny tensor-core product
- * (axq8_linear_q8act_s), A8 with M > 32, N >= 128 and K % 128 == 0 the tcgen05
- * product (axq8_linear_q8act_t), other A8 shapes up to M = 64 the skinny one;
- * everything else the streaming GEMV kernel (axq8_linear_path tells which). */
+ * must not overlap.  A8 with 8 < M <= 64 runs the skinny tensor-core product
+ * (axq8_linear_q8act_s), A8 with M > 64, N >= 128 and K % 128 == 0 the tcgen05
+ * product (axq8_linear_q8act_t); everything else the streaming GEMV kernel
+ * (axq8_linear_path tells which). */
 int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int act_mode,
                 void* stream);
 
