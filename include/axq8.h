@@ -109,7 +109,9 @@ int axq8_linear_path(const axq8_weight_t* w, int64_t M, int act_mode);
 /* The same product for decode widths (1 <= M <= 64, any N, K % 32 == 0) with
  * mma.sync m16n8k32 int8 and register accumulators (linear_from_gguf,
  * linear.cpp:27-71, for batched decode); inputs from axq8_quantize_act_t.
- * Exact int32 block dots; fp32 combination acc += (D_b*dw)*dx per block. */
+ * Exact int32 block dots; fp32 combination acc += (D_b*dw)*dx per block.
+ * Uses no device workspace (the K splits of a row tile are combined in shared
+ * memory within one thread-block cluster) and is deterministic run to run. */
 int axq8_linear_q8act_s(const axq8_weight_t* w, const int8_t* xq, const float* dxT, int64_t M,
                         const float* residual, float* y, void* stream);
 
