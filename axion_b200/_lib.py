@@ -1,4 +1,4 @@
-"""ctypes binding of libaxq8.so, the C ABI declared in include/axq8.h.
+"""ctypes binding of libaxq8.so, the C ABI declared in include/axq8.h, axdec.h and axkv.h.
 
 Loading fails loudly: there is no CPU fallback for any entry point.  If the
 shared library is missing, build it with ``python -m axion_b200.build``.
@@ -34,6 +34,14 @@ class axq8_weight_t(C.Structure):
         ("row_stride", C.c_int64),
         ("owns", C.c_int32),
         ("device", C.c_int32),
+    ]
+
+
+class axkv_cache_t(C.Structure):
+    _fields_ = [
+        ("k_pages", C.c_void_p), ("v_pages", C.c_void_p), ("block_table", C.c_void_p),
+        ("n_pages", C.c_int32), ("max_blocks", C.c_int32), ("n_kv_heads", C.c_int32),
+        ("head_dim", C.c_int32), ("page_tokens", C.c_int32), ("kv_fp32", C.c_int32),
     ]
 
 
@@ -87,6 +95,18 @@ SIGNATURES: dict[str, tuple] = {
     "axdec_step_kernels": (_I32, [_P, _I32]),
     "axdec_tp_unique_id": (_I32, [_P, _I64]),
     "axdec_tp_connect": (_I32, [_P, _P]),
+    "axkv_pages_bytes": (_I64, [C.POINTER(axkv_cache_t)]),
+    "axkv_paged_append": (_I32, [C.POINTER(axkv_cache_t), _P, _P, _I32, _P, _P, _P]),
+    "axkv_decode_attn_workspace": (_I64, [C.POINTER(axkv_cache_t), _I32, _I32]),
+    "axkv_paged_decode_attn": (_I32, [C.POINTER(axkv_cache_t), _P, _I32, _I32, _P, _P, _P, _I64,
+                                      _P]),
+    "axkv_paged_prefill_attn": (_I32, [C.POINTER(axkv_cache_t), _P, _I64, _I32, _I32, _I32, _I32,
+                                       _P, _P, _P, _P]),
+    "axdec_set_prefill": (_I32, [_P, _I32]),
+    "axdec_prefill_batched": (_I32, [_P, _I32]),
+    "axdec_prefill": (_I32, [_P, _P, _I32, _I32, _P]),
+    "axdec_decode_step": (_I32, [_P, _P, _I32, _P, _P, _P]),
+    "axdec_decode_continue": (_I32, [_P, _P, _I32, _I32, _P, C.POINTER(C.c_float), _P]),
     "axq8_status_read": (_I32, [C.POINTER(C.c_int)]),
     "axq8_status_clear": (_I32, []),
     "axq8_last_error": (C.c_char_p, []),

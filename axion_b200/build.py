@@ -90,12 +90,45 @@ def build(force: bool = False, jobs: int | None = None) -> Path:
     return LIB
 
 
+CPP_SRC = PKG / "cpp" / "axion_b200.cpp"
+CPP_LIB = PKG / "libaxion_b200_cpp.so"
+
+
+def build_cpp(ref_include: str | Path, force: bool = False) -> Path:
+    """The C++ boundary (include/axion_b200.hpp) for the reference's runtime:
+    compiled against the reference's own headers (its inference/cpp tree,
+    `ref_include`), linked to libaxq8.so and the CUDA runtime.  The symbols of
+    the reference's Tensor factory stay undefined here: the runtime that loads
+    the library provides them."""
+    ref_include = Path(ref_include)
+    if not (ref_include / "core" / "tensor.hpp").exists():
+        raise RuntimeError(f"reference headers not found under {ref_include}")
+    lib = build()
+    deps = [CPP_SRC, ROOT / "include" / "axion_b200.hpp", ROOT / "include" / "axq8.h", lib]
+    if not force and CPP_LIB.exists() and CPP_LIB.stat().st_mtime >= max(
+            d.stat().st_mtime for d in deps):
+        return CPP_LIB
+    cuda = Path(nvcc()).resolve().parent.parent
+    cmd = ["g++", "-std=c++17", "-O2", "-fPIC", "-shared", "-o", str(CPP_LIB), str(CPP_SRC),
+           f"-I{ROOT / 'include'}", f"-I{ref_include}", f"-I{cuda / 'include'}",
+           f"-L{PKG}", "-laxq8", f"-L{cuda / 'lib64'}", "-lcudart",
+           "-Wl,-rpath,$ORIGIN", f"-Wl,-rpath,{cuda / 'lib64'}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"g++ failed for {CPP_SRC.name}:\n{r.stdout}\n{r.stderr}")
+    return CPP_LIB
+
+
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("-j", type=int, default=None)
+    ap.add_argument("--cpp", metavar="REF_INCLUDE", default=None,
+                    help="also build the C++ boundary against the reference's inference/cpp tree")
     args = ap.parse_args()
     print(build(args.force, args.j))
+    if args.cpp:
+        print(build_cpp(args.cpp, args.force))
     return 0
 
 

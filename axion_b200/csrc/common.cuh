@@ -166,6 +166,22 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
     return d;
 }
 
+// Loads of data that another kernel of the same stream produced.  Kernels here
+// are launched with programmatic dependent launch: a kernel starts while its
+// predecessors still run and only griddepcontrol.wait orders it after them.
+// The read-only (non-coherent) path that __ldg and `const __restrict__`
+// pointers allow assumes the data does not change for the kernel's lifetime,
+// which no longer holds, and was measured to return stale values; these
+// loads go through L2 (ld.global.cg), which the wait makes coherent.
+__device__ __forceinline__ float ld_cg(const float* p) { return __ldcg(p); }
+__device__ __forceinline__ int ld_cg(const int* p) { return __ldcg(p); }
+__device__ __forceinline__ float2 ld_cg2(const float* p) {
+    return __ldcg(reinterpret_cast<const float2*>(p));
+}
+__device__ __forceinline__ float4 ld_cg4(const float* p) {
+    return __ldcg(reinterpret_cast<const float4*>(p));
+}
+
 __device__ inline int q8_round(float v) {
     float r = roundf(v);
     r = fminf(fmaxf(r, -127.0f), 127.0f);

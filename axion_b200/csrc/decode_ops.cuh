@@ -30,12 +30,12 @@ namespace axq8 {
 
 // ---- embedding ----------------------------------------------------------------
 // h[m, :] = dequantized row tokens[m] of token_embd (repacked Q8_0 rows).
-__global__ void embed_kernel(const uint8_t* __restrict__ rows, int64_t rs, int H, int V,
+static __global__ void embed_kernel(const uint8_t* __restrict__ rows, int64_t rs, int H, int V,
                              const int* __restrict__ tokens, float* __restrict__ h, int* status) {
     pdl_launch_dependents();
     pdl_wait();
     const int m = blockIdx.x;
-    int tok = tokens[m];
+    int tok = ld_cg(tokens + m);
     if (tok < 0 || tok >= V) {
         if (threadIdx.x == 0) record_status(status, AXQ8_ERR_INVALID);
         tok = 0;
@@ -77,6 +77,13 @@ __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
     v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
     v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
 }
+// load8 of data another kernel produced (coherent, through L2)
+__device__ __forceinline__ void load8_cg(const float* p, float (&v)[8]) {
+    const float4 a = ld_cg4(p);
+    const float4 b = ld_cg4(p + 4);
+    v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w;
+    v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+}
 __device__ __forceinline__ void store8(float* p, const float (&v)[8]) {
     *reinterpret_cast<float4*>(p) = make_float4(v[0], v[1], v[2], v[3]);
     *reinterpret_cast<float4*>(p + 4) = make_float4(v[4], v[5], v[6], v[7]);
@@ -114,7 +121,7 @@ __global__ void __launch_bounds__(1024) rmsnorm_kernel(const float* __restrict__
     for (int u = 0; u < kNormUnits; u++) {
         const int j = threadIdx.x + u * blockDim.x;
         if (j < nu) {
-            load8(xr + 8 * j, v[u]);
+            load8_cg(xr + 8 * j, v[u]);
         } else {
 #pragma unroll
             for (int e = 0; e < 8; e++) v[u][e] = wv[u][e] = 0.0f;
@@ -271,7 +278,7 @@ __global__ void attn_decode_kernel(const float* __restrict__ qkv, int ldq,
     pdl_wait();
     // a position past the page table was already reported by the KV append;
     // never read beyond the table
-    const int ctx = min(pos[m] + 1, max_blocks * B);
+    const int ctx = min(ld_cg(pos + m) + 1, max_blocks * B);
     const int nblk = (ctx + B - 1) / B;
     const int b1 = min(nblk, b0 + bps);
     for (int i = threadIdx.x; i < G * HD / 4; i += blockDim.x)
@@ -463,7 +470,7 @@ __global__ void __launch_bounds__(kAttnTcWarps * 32)
         pg[i] = b0 + i < max_blocks ? block_table[m * max_blocks + b0 + i] : 0;
     pdl_launch_dependents();
     pdl_wait();
-    const int ctx = min(pos[m] + 1, max_blocks * B);
+    const int ctx = min(ld_cg(pos + m) + 1, max_blocks * B);
     const int nblk = (ctx + B - 1) / B;
     const int b1 = min(nblk, b0 + bps);
     __syncthreads();   // pg visible
@@ -479,7 +486,7 @@ __global__ void __launch_bounds__(kAttnTcWarps * 32)
                 const int col = k * 16 + 2 * t + ((r & 2) ? 8 : 0);
                 float x = 0.0f, y = 0.0f;
                 if (row < G) {
-                    const float2 v = *reinterpret_cast<const float2*>(q0 + (int64_t)row * HD + col);
+                    const float2 v = ld_cg2(q0 + (int64_t)row * HD + col);
                     x = v.x;
                     y = v.y;
                 }
@@ -659,15 +666,18 @@ __global__ void __launch_bounds__(kAttnTcWarps * 32)
         attn_merge_head<HD, Q8>(part, m, n_heads, kvh * G + hh, nsplit, out, xq, dx, dxt, lane);
 }
 
-// ---- RoPE + KV append over product rows (wide batches) ---------------------------
+// ---- RoPE + KV append over product rows (wide batches, prefill chunks) ----------
 // The tensor-core product writes qkv [M][Nq + 2 Nkv] with the Q and K rows of
 // each head in the (j, j + hd/2) pair order of the permuted weight.  One warp
-// per (sequence, head): it reads the whole head, then rotates Q back into
-// natural order in place and writes K (rotated) and V into the KV page of the
-// sequence's position, as the GEMV's RoPE/KV epilogue does.
+// per (row, head): it reads the whole head, then rotates Q back into natural
+// order in place and writes K (rotated) and V into the KV page of the row's
+// position, as the GEMV's RoPE/KV epilogue does.  Decode steps (T == 0): row
+// m is sequence m at position pos[m].  Prefill chunks (T > 0): row m is
+// sequence m / T at position p0 + m % T.
 template <typename KV>
 __global__ void rope_kv_rows_kernel(float* __restrict__ qkv, int M, int n_heads, int n_kv, int hd,
-                                   const int* __restrict__ pos, const float2* __restrict__ rope,
+                                   const int* __restrict__ pos, int T, int p0,
+                                   const float2* __restrict__ rope,
                                    int max_ctx, const int* __restrict__ block_table, int max_blocks,
                                    int B, KV* __restrict__ kc, KV* __restrict__ vc,
                                    int* __restrict__ status) {
@@ -679,17 +689,18 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ qkv, int M, int n_heads,
     if (gw >= M * heads) return;
     const int m = gw / heads, hh = gw % heads;
     const int half = hd / 2;
-    const int p = pos[m];
+    const int seq = T > 0 ? m / T : m;
+    const int p = T > 0 ? p0 + m % T : ld_cg(pos + m);
     if (p < 0 || p >= max_ctx) {
         if (lane == 0) record_status(status, AXQ8_ERR_INVALID);
         return;
     }
-    const int page = block_table[m * max_blocks + p / B], slot = p % B;
+    const int page = block_table[seq * max_blocks + p / B], slot = p % B;
     const int ldq = (n_heads + 2 * n_kv) * hd;
     float* row = qkv + (int64_t)m * ldq + (int64_t)hh * hd;
     if (hh >= n_heads + n_kv) {                       // V: natural order, copy
         KV* dst = vc + (((int64_t)page * n_kv + (hh - n_heads - n_kv)) * B + slot) * hd;
-        for (int d = lane; d < hd; d += 32) kv_store(dst + d, row[d]);
+        for (int d = lane; d < hd; d += 32) kv_store(dst + d, ld_cg(row + d));
         return;
     }
     // pairs j = lane, lane + 32 (hd <= 128)
@@ -698,8 +709,9 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ qkv, int M, int n_heads,
     for (int t = 0; t < 2; t++) {
         const int j = lane + 32 * t;
         if (j < half) {
-            v0[t] = row[2 * j];
-            v1[t] = row[2 * j + 1];
+            const float2 pr = ld_cg2(row + 2 * j);
+            v0[t] = pr.x;
+            v1[t] = pr.y;
         }
     }
     __syncwarp();
@@ -722,10 +734,262 @@ __global__ void rope_kv_rows_kernel(float* __restrict__ qkv, int M, int n_heads,
     }
 }
 
+// ---- batched prefill: prompt tokens of a chunk ------------------------------------
+// ptok[s * T + t] = feed[s * feed_len + p0 + t]: the chunk's rows, sequence-major.
+static __global__ void gather_chunk_tokens_kernel(const int* __restrict__ feed, int feed_len, int n_seq,
+                                           int T, int p0, int* __restrict__ ptok) {
+    pdl_launch_dependents();
+    pdl_wait();
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= n_seq * T) return;
+    ptok[i] = ld_cg(feed + (int64_t)(i / T) * feed_len + p0 + i % T);
+}
+
+// ---- causal attention over a prompt chunk (batched prefill) ----------------------
+// Reference: mha_attention / sdpa_causal (inference/cpp/runtime/mha.cpp:126-198):
+// query position i of a head attends to keys 0..i of its GQA kv head
+// (kv = h / (n_head / n_kv)), scores scaled by 1/sqrt(hd) after the dot,
+// max-subtracted softmax, out = sum p*v / sum p.
+//
+// The chunk's rows r = s * T + t hold sequence s at position p0 + t; its K and
+// V (and those of every earlier position) are already in the fp16 pages.
+// Grid (tiles * HG, n_kv, n_seq) with HG = G / Gc head groups of Gc = min(G, 8)
+// heads; 8 warps per CTA, warp w serving query head (w % Gc) of the group for
+// the 16 positions tile*TQ + 16*(w / Gc) .. +15 (TQ = 16 * 8 / Gc positions per
+// CTA), so the G heads of a kv head share every staged page.  The CTA walks
+// the pages 0 .. of its last position in stages of kPrefPages pages (K and V
+// by cp.async, double buffered, rows XOR-swizzled by 16-byte chunk for
+// conflict-free ldmatrix), each warp skipping pages past its own positions.
+// Per page and warp, as the decode kernel above: S [16 positions x 16 keys] =
+// Q K^T and O += P V with mma.sync m16n8k16, Q and P split into an fp16 high
+// part and an fp16 residual (fp32 accuracy against the exact fp16 K, V), the
+// causal mask key > position applied to the scaled scores, online softmax
+// with expf.  The output row (position, head) is divided by its sum and, with
+// Q8, quantized to A8 in 32-dim blocks (transposed scales, pitch dxt) for the
+// O projection, else stored as fp32 rows of `out`.
+constexpr int kPrefWarps = 8;
+constexpr int kPrefPages = 4;
+template <int HD>
+constexpr size_t attn_prefill_smem_bytes() {
+    return (size_t)2 /*buffers*/ * kPrefPages * 2 /*K,V*/ * 16 * HD * 2;
+}
+
+template <int HD, bool Q8>
+__global__ void __launch_bounds__(kPrefWarps * 32)
+    attn_prefill_kernel(const float* __restrict__ qkv, int ldq, int T, int p0,
+                        const __half* __restrict__ kc, const __half* __restrict__ vc,
+                        const int* __restrict__ block_table, int max_blocks, int n_kv, int G,
+                        float scale, int8_t* __restrict__ xq, int ldo, float* __restrict__ dxT,
+                        int dxt, float* __restrict__ out) {
+    constexpr int B = 16;
+    constexpr int KS = HD / 16;          // k-steps of the score product
+    constexpr int NT = HD / 8;           // n-tiles (8 dims) of the output
+    constexpr int CH = HD / 8;           // 16-byte chunks per K/V row
+    constexpr int PAGE = B * HD;         // halves per K (or V) page
+    constexpr int SP = kPrefPages;
+    extern __shared__ __align__(16) uint8_t pf_sm[];
+    __half* stage = reinterpret_cast<__half*>(pf_sm);   // [2][SP][K,V][B][HD]
+    const uint32_t stage_s = smem_u32(stage);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int Gc = G < 8 ? G : 8, HG = G / Gc;
+    const int TQ = 16 * (kPrefWarps / Gc);
+    const int tile = blockIdx.x / HG, hgrp = blockIdx.x % HG;
+    const int kvh = blockIdx.y, s = blockIdx.z;
+    const int head = kvh * G + hgrp * Gc + warp % Gc;
+    const int t0 = tile * TQ + (warp / Gc) * 16;          // this warp's first chunk position
+    const int cta_end = min(T, tile * TQ + TQ);           // the CTA's positions end here
+    const int npages = (p0 + cta_end + B - 1) / B;         // keys 0 .. p0 + cta_end - 1
+    const int nst = (npages + SP - 1) / SP;
+    const bool active = t0 < T && warp / Gc < kPrefWarps / Gc;
+    const int my_last = p0 + min(t0 + 15, T - 1);          // last position of this warp
+    const int qp0 = p0 + t0 + g, qp1 = qp0 + 8;            // positions of rows g, g + 8
+    pdl_launch_dependents();
+    pdl_wait();
+    const int* bt = block_table + (int64_t)s * max_blocks;
+    auto issue = [&](int st) {
+        __half* buf = stage + (size_t)(st & 1) * SP * 2 * PAGE;
+        for (int c = threadIdx.x; c < SP * B * CH; c += blockDim.x) {
+            const int j = c / (B * CH), r = (c / CH) % B, ch = c % CH;
+            const int pg = st * SP + j;
+            if (pg >= npages) continue;
+            const int64_t off = (((int64_t)bt[pg] * n_kv + kvh) * B + r) * HD + ch * 8;
+            const int sw = r * HD + ((ch ^ (r & 7)) * 8);
+            __half* kb = buf + (size_t)j * 2 * PAGE;
+            cp_async16(kb + sw, kc + off);
+            cp_async16(kb + PAGE + sw, vc + off);
+        }
+    };
+    // Q fragments: rows = positions t0 + g (+8) of `head`, fp16 high and residual
+    uint32_t qh[KS][4], ql[KS][4];
+    {
+#pragma unroll
+        for (int k = 0; k < KS; k++) {
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int tr = t0 + g + ((r & 1) ? 8 : 0);
+                const int col = k * 16 + 2 * t + ((r & 2) ? 8 : 0);
+                float x = 0.0f, y = 0.0f;
+                if (active && tr < T) {
+                    const float2 v =
+                        ld_cg2(qkv + ((int64_t)s * T + tr) * ldq + (int64_t)head * HD + col);
+                    x = v.x;
+                    y = v.y;
+                }
+                split_pair(x, y, qh[k][r], ql[k][r]);
+            }
+        }
+    }
+    float o[NT][4];
+#pragma unroll
+    for (int n = 0; n < NT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float mrun[2] = {-CUDART_INF_F, -CUDART_INF_F}, lrun[2] = {0.0f, 0.0f};
+    issue(0);
+    cp_async_commit();
+    for (int st = 0; st < nst; st++) {
+        if (st + 1 < nst) {
+            issue(st + 1);
+            cp_async_commit();
+            cp_async_wait_group<1>();
+        } else {
+            cp_async_wait_group<0>();
+        }
+        __syncthreads();   // stage st visible to every warp
+#pragma unroll 1
+        for (int j = 0; j < SP; j++) {
+            const int pg = st * SP + j;
+            if (!active || pg >= npages || pg * B > my_last) break;   // warp-uniform
+            const uint32_t kb = stage_s + (uint32_t)((((st & 1) * SP + j) * 2 * PAGE) * 2);
+            const uint32_t vb = kb + PAGE * 2;
+            float sc[2][4] = {{0.0f, 0.0f, 0.0f, 0.0f}, {0.0f, 0.0f, 0.0f, 0.0f}};
+            {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int tok = rr + ((mi >> 1) << 3);
+#pragma unroll
+                for (int k = 0; k < KS; k++) {
+                    const int ch = k * 2 + (mi & 1);
+                    uint32_t kf[4];
+                    ldsm_x4(kf, kb + (uint32_t)((tok * HD + ((ch ^ (tok & 7)) * 8)) * 2));
+                    mma_f16_16816(sc[0], qh[k], kf[0], kf[1]);
+                    mma_f16_16816(sc[0], ql[k], kf[0], kf[1]);
+                    mma_f16_16816(sc[1], qh[k], kf[2], kf[3]);
+                    mma_f16_16816(sc[1], ql[k], kf[2], kf[3]);
+                }
+            }
+            float p[2][4];
+#pragma unroll
+            for (int hr = 0; hr < 2; hr++) {
+                const int qp = hr ? qp1 : qp0;
+                float mt = -CUDART_INF_F;
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        const int key = pg * B + n * 8 + 2 * t + jj;
+                        float& v = sc[n][2 * hr + jj];
+                        v = key <= qp ? __fmul_rn(v, scale) : -CUDART_INF_F;
+                        mt = fmaxf(mt, v);
+                    }
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 1));
+                mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 2));
+                // page 0 holds key 0 <= every position, so mrun is finite after it
+                const float mnew = fmaxf(mrun[hr], mt);
+                const float corr = mrun[hr] == -CUDART_INF_F ? 0.0f : expf(mrun[hr] - mnew);
+                float ps = 0.0f;
+#pragma unroll
+                for (int n = 0; n < 2; n++)
+#pragma unroll
+                    for (int jj = 0; jj < 2; jj++) {
+                        const float v = sc[n][2 * hr + jj];
+                        const float e = v == -CUDART_INF_F ? 0.0f : expf(v - mnew);
+                        p[n][2 * hr + jj] = e;
+                        ps += e;
+                    }
+                lrun[hr] = fmaf(lrun[hr], corr, ps);
+                mrun[hr] = mnew;
+#pragma unroll
+                for (int n = 0; n < NT; n++) {
+                    o[n][2 * hr] *= corr;
+                    o[n][2 * hr + 1] *= corr;
+                }
+            }
+            uint32_t ph[4], pl[4];
+            split_pair(p[0][0], p[0][1], ph[0], pl[0]);
+            split_pair(p[0][2], p[0][3], ph[1], pl[1]);
+            split_pair(p[1][0], p[1][1], ph[2], pl[2]);
+            split_pair(p[1][2], p[1][3], ph[3], pl[3]);
+            {
+                const int mi = lane >> 3, rr = lane & 7;
+                const int tok = rr + ((mi & 1) << 3);
+#pragma unroll
+                for (int dn = 0; dn < HD / 16; dn++) {
+                    const int ch = dn * 2 + (mi >> 1);
+                    uint32_t vf[4];
+                    ldsm_x4_t(vf, vb + (uint32_t)((tok * HD + ((ch ^ (tok & 7)) * 8)) * 2));
+                    mma_f16_16816(o[2 * dn], ph, vf[0], vf[1]);
+                    mma_f16_16816(o[2 * dn], pl, vf[0], vf[1]);
+                    mma_f16_16816(o[2 * dn + 1], ph, vf[2], vf[3]);
+                    mma_f16_16816(o[2 * dn + 1], pl, vf[2], vf[3]);
+                }
+            }
+        }
+        __syncthreads();   // every warp is done with buffer st & 1 before it is refilled
+    }
+    if (!active) return;
+#pragma unroll
+    for (int hr = 0; hr < 2; hr++) {
+        lrun[hr] += __shfl_xor_sync(0xffffffffu, lrun[hr], 1);
+        lrun[hr] += __shfl_xor_sync(0xffffffffu, lrun[hr], 2);
+    }
+    // out = O / l, quantized per 32-dim block (n-tiles 4b .. 4b + 3; the quad
+    // t = 0..3 holds the block's 32 values of each row)
+#pragma unroll
+    for (int hr = 0; hr < 2; hr++) {
+        const int tr = t0 + g + 8 * hr;
+        const bool ok = tr < T;
+        const int64_t row = (int64_t)s * T + tr;
+#pragma unroll
+        for (int b = 0; b < HD / 32; b++) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                v[2 * i] = __fdiv_rn(o[4 * b + i][2 * hr], lrun[hr]);
+                v[2 * i + 1] = __fdiv_rn(o[4 * b + i][2 * hr + 1], lrun[hr]);
+            }
+            if (!Q8) {   // fp32 rows [n_seq * T][ldo]
+                if (ok) {
+                    float* orow = out + row * ldo + (int64_t)head * HD + 32 * b;
+#pragma unroll
+                    for (int i = 0; i < 4; i++)
+                        *reinterpret_cast<float2*>(orow + 8 * i + 2 * t) = make_float2(v[2 * i], v[2 * i + 1]);
+                }
+                continue;
+            }
+            uint32_t ab = 0;
+#pragma unroll
+            for (int e = 0; e < 8; e++) ab = max(ab, __float_as_uint(fabsf(v[e])));
+            ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 1));
+            ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 2));
+            const float amax = __uint_as_float(ab);
+            const float id = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
+            if (!ok) continue;
+            int8_t* qrow = xq + row * ldo + (int64_t)head * HD + 32 * b;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const uint32_t q0 = (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[2 * i], id));
+                const uint32_t q1 = (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[2 * i + 1], id));
+                *reinterpret_cast<uint16_t*>(qrow + 8 * i + 2 * t) = (uint16_t)(q0 | (q1 << 8));
+            }
+            if (t == 0)
+                dxT[((int64_t)head * HD / QK + b) * dxt + row] = __fdiv_rn(amax, 127.0f);
+        }
+    }
+}
+
 // ---- greedy argmax over logit rows (wide batches) ---------------------------------
 // Grid (chunks, M): each CTA folds its part of row m into amax_key[m] (zero
 // before; argmax_advance_kernel consumes and clears it).
-__global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int idx_offset,
+static __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int idx_offset,
                                    unsigned long long* __restrict__ amax_key) {
     pdl_launch_dependents();
     pdl_wait();
@@ -733,7 +997,7 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int 
     const float* row = logits + (int64_t)m * V;
     unsigned long long best = 0ull;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
-        const unsigned long long k = argmax_key(row[i], i + idx_offset);
+        const unsigned long long k = argmax_key(ld_cg(row + i), i + idx_offset);
         best = k > best ? k : best;
     }
 #pragma unroll
@@ -750,23 +1014,23 @@ __global__ void argmax_rows_kernel(const float* __restrict__ logits, int V, int 
 // all-reduce over ranks one thread performs the advance of the argmax epilogue: record the token,
 // feed the next input (prompt token or the argmax), move the position, and
 // zero the key for the next step.
-__global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key, int M,
+static __global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key, int M,
                                       int* __restrict__ pos, int* __restrict__ tokens,
                                       const int* __restrict__ feed, const int* __restrict__ ctl,
                                       int* __restrict__ out_tokens, int* __restrict__ argmax_out) {
     pdl_launch_dependents();
     pdl_wait();
     if (threadIdx.x != 0 || blockIdx.x != 0) return;
-    const int n_prompt = ctl[0], feed_len = ctl[1], max_out = ctl[2];
+    const int n_prompt = ld_cg(ctl), feed_len = ld_cg(ctl + 1), max_out = ld_cg(ctl + 2);
     for (int m = 0; m < M; m++) {
-        const unsigned long long k = amax_key[m];
+        const unsigned long long k = __ldcg(amax_key + m);
         amax_key[m] = 0ull;
         const int idx = k == 0ull ? 0 : argmax_key_index(k);
-        const int p = pos[m];
+        const int p = ld_cg(pos + m);
         const int np = p + 1;
         argmax_out[m] = idx;
         if (np >= n_prompt && np - n_prompt < max_out) out_tokens[m * max_out + (np - n_prompt)] = idx;
-        tokens[m] = np < feed_len ? feed[m * feed_len + np] : idx;
+        tokens[m] = np < feed_len ? ld_cg(feed + m * feed_len + np) : idx;
         pos[m] = np;
     }
 }
@@ -790,8 +1054,8 @@ __global__ void silu_mul_kernel(const float* __restrict__ gu, int F, int M,
     float g[8], u[8], a[8];
     if (valid) {
         float p[16];
-        load8(gu + (int64_t)m * 2 * F + 16 * c, *reinterpret_cast<float(*)[8]>(p));
-        load8(gu + (int64_t)m * 2 * F + 16 * c + 8, *reinterpret_cast<float(*)[8]>(p + 8));
+        load8_cg(gu + (int64_t)m * 2 * F + 16 * c, *reinterpret_cast<float(*)[8]>(p));
+        load8_cg(gu + (int64_t)m * 2 * F + 16 * c + 8, *reinterpret_cast<float(*)[8]>(p + 8));
 #pragma unroll
         for (int e = 0; e < 8; e++) {
             g[e] = p[2 * e];

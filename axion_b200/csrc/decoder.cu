@@ -103,6 +103,18 @@ struct axdec_model {
     MmaScratch mma_sc;                        // split-K scratch of the wide-batch products
     cudaStream_t cap_stream = nullptr;
     std::map<int, Graph> graphs;  // per batch size
+    // batched prefill (A8): buffers of one prompt chunk, allocated on first use
+    int prefill_mode = 1;         // 1: batched where supported, 0: through the decode step
+    int pre_cap = 0;              // rows the chunk buffers hold
+    float* ph = nullptr;          // [cap, H] residual stream of the chunk
+    int8_t* pxq = nullptr;        // [cap, maxK] A8 activations
+    float* pdx = nullptr;         // [maxK/32, pitch(cap)] their block scales (transposed)
+    float* pqkv = nullptr;        // [cap, Nqkv]
+    float* pgu = nullptr;         // [cap, 2F] interleaved gate/up
+    int* ptok = nullptr;          // [cap] token ids of the chunk rows
+    MmaScratch pre_sc;            // split-K scratch of the chunk products (grown on demand)
+    // decode session of axdec_prefill / axdec_decode_step
+    int sess_seq = 0, sess_pos = -1;
 };
 
 namespace {
@@ -441,7 +453,7 @@ int launch_step_wide(axdec_model* m, int M, cudaStream_t s) {
         if ((rc = wide_linear(m, Ly.qkv, m->Nqkv, H, M, nullptr, m->qkv, s))) return rc;
         AXQ8_CUDA_TRY(launch_k(rope_kv_rows_kernel<KV>, dim3((M * heads + 7) / 8), dim3(256), 0, s,
                                true, m->qkv, M, c.n_heads, c.n_kv_heads, hd, (const int*)m->pos,
-                               (const float2*)m->rope, c.max_ctx, (const int*)m->block_table,
+                               0, 0, (const float2*)m->rope, c.max_ctx, (const int*)m->block_table,
                                m->max_blocks, c.kv_block, (KV*)Ly.kc, (KV*)Ly.vc, ds->status),
                       "rope/kv launch");
         if (hd == 32) rc = launch_attention<KV, 32>(m, M, l, s, dxt);
@@ -603,6 +615,217 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
                            m->out_tokens, m->argmax),
                   "argmax advance launch");
     return AXQ8_OK;
+}
+
+// ---- batched prefill -------------------------------------------------------------
+// The prompt's positions run through the layers as one wide product per linear
+// per chunk (rows = sequences x positions, the tcgen05 product above 64 rows,
+// the skinny one up to 64), the chunk's K and V go to the pages, and a causal
+// attention kernel reads every earlier page: StreamingExecutor::execute_layer
+// (streaming_executor.cpp:110-238) and mha_attention (mha.cpp:167-198) for a
+// whole prompt, where ModelRunner::generate feeds the prompt one position at a
+// time (model_runner.cpp:291-295).  No logits: the last prompt position goes
+// through the decode step, which yields the first generated token.
+constexpr int kPrefillRows = 4096;   // rows of one chunk when every linear tiles on tcgen05
+
+bool all_mma_ok(const axdec_model* m, int64_t M) {
+    const axdec_config_t& c = m->c;
+    const int64_t H = c.hidden, F = c.ffn;
+    return mma_shape_ok(m->Nqkv, H, M) && mma_shape_ok(H, m->Nq, M) && mma_shape_ok(2 * F, H, M) &&
+           mma_shape_ok(H, F, M);
+}
+
+// Whether prompts of n_seq sequences can take the batched prefill.
+bool prefill_supported(const axdec_model* m, int n_seq) {
+    const axdec_config_t& c = m->c;
+    const int G = c.n_heads / c.n_kv_heads;
+    if (m->prefill_mode == 0 || c.act_mode != AXQ8_ACT_Q8 || c.kv_fp32) return false;
+    if (c.head_dim != 64 && c.head_dim != 128) return false;
+    if (G > 8 && G % 8) return false;
+    return n_seq <= kMmqMaxM || all_mma_ok(m, kPrefillRows);
+}
+
+// Positions of one chunk: as many as fit kPrefillRows rows (64 rows when some
+// linear does not tile on tcgen05), at least one.
+// AXDEC_PREFILL_ROWS = r (1 .. the cap) sets a smaller chunk (tests of the
+// chunk boundaries, tuning runs).
+int prefill_chunk_positions(const axdec_model* m, int n_seq, int n_tok) {
+    int cap = all_mma_ok(m, kPrefillRows) ? kPrefillRows : kMmqMaxM;
+    const char* e = getenv("AXDEC_PREFILL_ROWS");
+    const int r = e ? atoi(e) : 0;
+    if (r >= 1 && r < cap) cap = r;
+    return std::max(1, std::min(n_tok, cap / n_seq));
+}
+
+// Chunk buffers for the largest chunk any prompt of this model can form (a
+// chunk holds n_seq * T <= the chunk cap rows, or n_seq rows when T = 1).
+int prefill_alloc(axdec_model* m) {
+    if (m->pre_cap) return AXQ8_OK;
+    const axdec_config_t& c = m->c;
+    const int cap = all_mma_ok(m, kPrefillRows) ? kPrefillRows : kMmqMaxM;
+    const int rows = (int)std::max<int64_t>(std::min<int64_t>(cap, (int64_t)c.max_batch * c.max_ctx),
+                                            c.max_batch);
+    const int H = c.hidden, F = c.ffn;
+    const int maxK = std::max(std::max(H, F), m->Nq);
+    int rc = AXQ8_OK;
+    m->ph = (float*)dalloc(m, sizeof(float) * (size_t)rows * H, &rc);
+    m->pxq = (int8_t*)dalloc(m, (size_t)rows * maxK, &rc);
+    m->pdx = (float*)dalloc(m, sizeof(float) * mma_scale_pitch(rows) * (maxK / QK), &rc);
+    m->pqkv = (float*)dalloc(m, sizeof(float) * (size_t)rows * m->Nqkv, &rc);
+    m->pgu = (float*)dalloc(m, sizeof(float) * (size_t)rows * 2 * F, &rc);
+    m->ptok = (int*)dalloc(m, sizeof(int) * rows, &rc);
+    if (rc == AXQ8_OK) m->pre_cap = rows;
+    return rc;
+}
+
+// Split-K scratch for the chunk products at Mc rows (grown outside any capture).
+int prefill_scratch(axdec_model* m, int Mc) {
+    if (Mc <= kMmqMaxM) return AXQ8_OK;
+    const axdec_config_t& c = m->c;
+    const int64_t H = c.hidden, F = c.ffn;
+    const int64_t shapes[4][2] = {{m->Nqkv, H}, {H, m->Nq}, {2 * F, H}, {H, F}};
+    size_t part = 0;
+    int64_t cnt = 0;
+    for (auto& sh : shapes) {
+        size_t pb = 0;
+        int64_t cn = 0;
+        mma_split_needs(m->ds, sh[0], sh[1], Mc, &pb, &cn);
+        part = std::max(part, pb);
+        cnt = std::max(cnt, cn);
+    }
+    MmaScratch& sc = m->pre_sc;
+    if (part <= sc.part_bytes && cnt <= sc.counter_slots) return AXQ8_OK;
+    AXQ8_CUDA_TRY(cudaDeviceSynchronize(), "axdec: prefill scratch");
+    int rc = AXQ8_OK;
+    if (part > sc.part_bytes) {
+        sc.part = (float*)dalloc(m, part, &rc);
+        sc.part_bytes = rc == AXQ8_OK ? part : 0;
+    }
+    if (rc == AXQ8_OK && cnt > sc.counter_slots) {
+        sc.counters = (int*)dalloc(m, sizeof(int) * cnt, &rc);
+        sc.counter_slots = rc == AXQ8_OK ? cnt : 0;
+        if (rc == AXQ8_OK) AXQ8_CUDA_TRY(cudaMemset(sc.counters, 0, sizeof(int) * cnt), "axdec: counters");
+    }
+    return rc;
+}
+
+int prefill_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int Mc,
+                   const float* resid, float* y, cudaStream_t s) {
+    axq8_weight_t w = {};
+    w.rows = const_cast<uint8_t*>(rows);
+    w.N = N;
+    w.K = K;
+    w.row_stride = q8r_row_stride(K);
+    w.device = m->ds->device;
+    if (Mc <= kMmqMaxM) return mmq_linear(m->ds, &w, m->pxq, m->pdx, Mc, resid, y, N, s);
+    return mma_linear(m->ds, &w, m->pxq, m->pdx, Mc, resid, y, N, nullptr, s, &m->pre_sc);
+}
+
+template <int HD>
+int launch_attn_prefill(axdec_model* m, int layer, int n_seq, int T, int p0, int dxt,
+                        cudaStream_t s) {
+    const axdec_config_t& c = m->c;
+    const int G = c.n_heads / c.n_kv_heads;
+    const int Gc = std::min(G, 8), HG = G / Gc;
+    const int TQ = 16 * (kPrefWarps / Gc);
+    constexpr size_t smem = attn_prefill_smem_bytes<HD>();
+    auto kern = attn_prefill_kernel<HD, true>;
+    static int configured[64] = {0};
+    const int dev = m->ds->device < 64 ? m->ds->device : 63;
+    if (smem > 48 * 1024 && !configured[dev]) {
+        AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem),
+                      "prefill attention smem attribute");
+        configured[dev] = 1;
+    }
+    const float scale = 1.0f / std::sqrt((float)HD);   // mha.cpp:131
+    Layer& Ly = m->L[layer];
+    AXQ8_CUDA_TRY(launch_k(kern, dim3((unsigned)(((T + TQ - 1) / TQ) * HG), c.n_kv_heads, n_seq),
+                           dim3(kPrefWarps * 32), smem, s, true, (const float*)m->pqkv, m->Nqkv, T,
+                           p0, (const __half*)Ly.kc, (const __half*)Ly.vc,
+                           (const int*)m->block_table, m->max_blocks, c.n_kv_heads, G, scale,
+                           m->pxq, m->Nq, m->pdx, dxt, (float*)nullptr),
+                  "prefill attention launch");
+    return AXQ8_OK;
+}
+
+// Positions 0 .. n_tok - 1 of sequences 0 .. n_seq - 1, tokens from m->feed
+// ([n_seq][feed_len], uploaded by reset_run): KV pages written, no logits.
+int prefill_positions(axdec_model* m, int n_seq, int n_tok, int feed_len, cudaStream_t s) {
+    const axdec_config_t& c = m->c;
+    const int H = c.hidden, F = c.ffn, hd = c.head_dim;
+    const int T = prefill_chunk_positions(m, n_seq, n_tok);
+    int rc = prefill_alloc(m);
+    if (rc) return rc;
+    if (n_seq * T > m->pre_cap)
+        return fail(AXQ8_ERR_INVALID, "axdec: prefill chunk of %d rows above %d", n_seq * T, m->pre_cap);
+    DeviceState* ds = m->ds;
+    float* resid = m->rank == 0 ? m->ph : nullptr;
+    const int heads = c.n_heads + 2 * c.n_kv_heads;
+    const int threads = rmsnorm_threads(H);
+    const NcclApi* api = m->tp > 1 ? nccl_api() : nullptr;
+    if (m->tp > 1 && !api) return AXQ8_ERR_UNSUPPORTED;
+    for (int p0 = 0; p0 < n_tok; p0 += T) {
+        const int Tc = std::min(T, n_tok - p0), Mc = n_seq * Tc;
+        const int dxt = (int)mma_scale_pitch(Mc);
+        if ((rc = prefill_scratch(m, Mc))) return rc;
+        AXQ8_CUDA_TRY(launch_k(gather_chunk_tokens_kernel, dim3((Mc + 255) / 256), dim3(256), 0, s,
+                               true, (const int*)m->feed, feed_len, n_seq, Tc, p0, m->ptok),
+                      "prefill tokens launch");
+        AXQ8_CUDA_TRY(launch_k(embed_kernel, dim3(Mc), dim3(256), 0, s, true, (const uint8_t*)m->embd,
+                               m->rs_h, H, m->cf.vocab, (const int*)m->ptok, m->ph, ds->status),
+                      "prefill embed launch");
+        for (int l = 0; l < c.n_layers; l++) {
+            Layer& Ly = m->L[l];
+            AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<true>, dim3(Mc), dim3(threads), 0, s, true,
+                                   (const float*)m->ph, (const float*)Ly.attn_norm, H, c.rms_eps,
+                                   (float*)nullptr, m->pxq, m->pdx, dxt),
+                          "prefill rmsnorm launch");
+            if ((rc = prefill_linear(m, Ly.qkv, m->Nqkv, H, Mc, nullptr, m->pqkv, s))) return rc;
+            AXQ8_CUDA_TRY(launch_k(rope_kv_rows_kernel<__half>, dim3((Mc * heads + 7) / 8), dim3(256), 0,
+                                   s, true, m->pqkv, Mc, c.n_heads, c.n_kv_heads, hd,
+                                   (const int*)nullptr, Tc, p0, (const float2*)m->rope, c.max_ctx,
+                                   (const int*)m->block_table, m->max_blocks, c.kv_block,
+                                   (__half*)Ly.kc, (__half*)Ly.vc, ds->status),
+                          "prefill rope/kv launch");
+            rc = hd == 64 ? launch_attn_prefill<64>(m, l, n_seq, Tc, p0, dxt, s)
+                          : launch_attn_prefill<128>(m, l, n_seq, Tc, p0, dxt, s);
+            if (rc) return rc;
+            if ((rc = prefill_linear(m, Ly.o, H, m->Nq, Mc, resid, m->ph, s))) return rc;
+            if (m->tp > 1 &&
+                (rc = nccl_check(api->AllReduce(m->ph, m->ph, (size_t)Mc * H, ncclFloat, ncclSum,
+                                                m->comm, s),
+                                 "axdec: prefill all-reduce")))
+                return rc;
+            AXQ8_CUDA_TRY(launch_k(rmsnorm_kernel<true>, dim3(Mc), dim3(threads), 0, s, true,
+                                   (const float*)m->ph, (const float*)Ly.ffn_norm, H, c.rms_eps,
+                                   (float*)nullptr, m->pxq, m->pdx, dxt),
+                          "prefill rmsnorm launch");
+            if ((rc = prefill_linear(m, Ly.gu, 2 * (int64_t)F, H, Mc, nullptr, m->pgu, s))) return rc;
+            AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, silu_grid(Mc, F), dim3(kSiluThreads), 0, s,
+                                   true, (const float*)m->pgu, F, Mc, (float*)nullptr, m->pxq, m->pdx,
+                                   dxt),
+                          "prefill silu launch");
+            if ((rc = prefill_linear(m, Ly.down, H, F, Mc, resid, m->ph, s))) return rc;
+            if (m->tp > 1 &&
+                (rc = nccl_check(api->AllReduce(m->ph, m->ph, (size_t)Mc * H, ncclFloat, ncclSum,
+                                                m->comm, s),
+                                 "axdec: prefill all-reduce")))
+                return rc;
+        }
+    }
+    return AXQ8_OK;
+}
+
+// Every sequence at position `p` with input token column `col` of the fed tokens.
+int set_positions(axdec_model* m, const int32_t* feed_host, int n_seq, int feed_len, int col, int p,
+                  cudaStream_t s) {
+    std::vector<int> tok(n_seq), pos(n_seq, p);
+    for (int i = 0; i < n_seq; i++) tok[i] = feed_host[(size_t)i * feed_len + col];
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->tokens, tok.data(), sizeof(int) * n_seq, cudaMemcpyHostToDevice, s),
+                  "axdec: tokens upload");
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->pos, pos.data(), sizeof(int) * n_seq, cudaMemcpyHostToDevice, s),
+                  "axdec: positions upload");
+    return AXQ8_OK;   // pageable sources: staged before the calls return
 }
 
 // Instantiate (once per batch size) the graph of one decode step.  The first
@@ -1014,6 +1237,16 @@ int axdec_generate(axdec_model_t* m, const int32_t* prompts, int32_t n_seq, int3
     int rc = get_graph(m, n_seq, &g);
     if (rc) return rc;
     if ((rc = reset_run(m, prompts, n_seq, n_prompt, n_prompt, n_new, s))) return rc;
+    m->sess_seq = 0;
+    m->sess_pos = -1;
+    int r0 = 0;
+    if (n_prompt >= 2 && prefill_supported(m, n_seq)) {
+        // prompt positions 0 .. n_prompt - 2 in one batched pass; the last
+        // prompt position goes through the step and yields the first token
+        if ((rc = prefill_positions(m, n_seq, n_prompt - 1, n_prompt, s))) return rc;
+        if ((rc = set_positions(m, prompts, n_seq, n_prompt, n_prompt - 1, n_prompt - 1, s))) return rc;
+        r0 = n_prompt - 1;
+    }
     cudaEvent_t e0 = nullptr, e1 = nullptr;
     if (decode_ms) {
         AXQ8_CUDA_TRY(cudaEventCreate(&e0), "event");
@@ -1021,7 +1254,7 @@ int axdec_generate(axdec_model_t* m, const int32_t* prompts, int32_t n_seq, int3
     }
     const int total = n_prompt - 1 + n_new;
     const size_t lbytes = sizeof(float) * (size_t)n_seq * m->c.vocab;
-    for (int r = 0; r < total; r++) {
+    for (int r = r0; r < total; r++) {
         if (decode_ms && r == n_prompt - 1) cudaEventRecord(e0, s);
         AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec: graph launch");
         if (logits_out && r >= n_prompt - 1) {
@@ -1058,6 +1291,8 @@ int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t
     if (rc) return rc;
     const int n_out = n_steps - n_prompt + 1;
     if ((rc = reset_run(m, tokens, n_seq, n_steps, n_prompt, n_out, s))) return rc;
+    m->sess_seq = 0;
+    m->sess_pos = -1;
     const size_t lbytes = sizeof(float) * (size_t)n_seq * m->c.vocab;
     for (int r = 0; r < n_steps; r++) {
         AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec: graph launch");
@@ -1067,6 +1302,126 @@ int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t
                           "axdec: logits copy");
     }
     AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec: forced");
+    return AXQ8_OK;
+}
+
+int axdec_set_prefill(axdec_model_t* m, int mode) {
+    if (!m || (mode != 0 && mode != 1)) return fail(AXQ8_ERR_INVALID, "axdec_set_prefill: bad argument");
+    m->prefill_mode = mode;
+    return AXQ8_OK;
+}
+
+int axdec_prefill_batched(const axdec_model_t* m, int32_t n_seq) {
+    return m && n_seq > 0 && n_seq <= m->c.max_batch && prefill_supported(m, n_seq) ? 1 : 0;
+}
+
+int axdec_prefill(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
+                  void* stream) {
+    if (!m || (!tokens && n_tok > 0)) return fail(AXQ8_ERR_INVALID, "axdec_prefill: null argument");
+    if (n_seq <= 0 || n_seq > m->c.max_batch || n_tok < 0 || n_tok >= m->c.max_ctx)
+        return fail(AXQ8_ERR_INVALID, "axdec_prefill: bad sizes (n_seq %d, n_tok %d, max_ctx %d)",
+                    n_seq, n_tok, m->c.max_ctx);
+    if (m->tp > 1 && !m->comm)
+        return fail(AXQ8_ERR_STATE, "axdec_prefill: tensor-parallel model not connected");
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaGraphExec_t g;
+    int rc = get_graph(m, n_seq, &g);
+    if (rc) return rc;
+    m->sess_seq = 0;
+    m->sess_pos = -1;
+    if (n_tok > 0) {
+        if ((rc = reset_run(m, tokens, n_seq, n_tok, n_tok + 1, 0, s))) return rc;
+        if (prefill_supported(m, n_seq)) {
+            if ((rc = prefill_positions(m, n_seq, n_tok, n_tok, s))) return rc;
+        } else {
+            for (int r = 0; r < n_tok; r++)
+                AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec: graph launch");
+        }
+    }
+    // the session continues at position n_tok with the caller's tokens: no
+    // fed tokens, no recorded outputs
+    std::vector<int> pos(n_seq, n_tok);
+    const int ctl[3] = {0, 0, 0};
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->pos, pos.data(), sizeof(int) * n_seq, cudaMemcpyHostToDevice, s),
+                  "axdec: positions upload");
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice, s),
+                  "axdec: ctl upload");
+    AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec_prefill");
+    m->sess_seq = n_seq;
+    m->sess_pos = n_tok;
+    return AXQ8_OK;
+}
+
+int axdec_decode_step(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t* next_tokens,
+                      float* logits_out, void* stream) {
+    if (!m || !tokens || !next_tokens) return fail(AXQ8_ERR_INVALID, "axdec_decode_step: null argument");
+    if (m->sess_pos < 0 || n_seq != m->sess_seq)
+        return fail(AXQ8_ERR_STATE, "axdec_decode_step: no session of %d sequences (call axdec_prefill)",
+                    n_seq);
+    if (m->sess_pos >= m->c.max_ctx)
+        return fail(AXQ8_ERR_INVALID, "axdec_decode_step: position %d reaches max_ctx %d", m->sess_pos,
+                    m->c.max_ctx);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaGraphExec_t g;
+    int rc = get_graph(m, n_seq, &g);
+    if (rc) return rc;
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->tokens, tokens, sizeof(int) * n_seq, cudaMemcpyHostToDevice, s),
+                  "axdec_decode_step: tokens upload");
+    AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec_decode_step: graph launch");
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(next_tokens, m->argmax, sizeof(int) * n_seq, cudaMemcpyDeviceToHost, s),
+                  "axdec_decode_step: tokens copy");
+    if (logits_out)
+        AXQ8_CUDA_TRY(cudaMemcpyAsync(logits_out, m->logits, sizeof(float) * (size_t)n_seq * m->c.vocab,
+                                      cudaMemcpyDeviceToHost, s),
+                      "axdec_decode_step: logits copy");
+    AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec_decode_step");
+    m->sess_pos++;
+    return AXQ8_OK;
+}
+
+int axdec_decode_continue(axdec_model_t* m, const int32_t* first_tokens, int32_t n_seq,
+                          int32_t n_steps, int32_t* out_tokens, float* decode_ms, void* stream) {
+    if (!m || !out_tokens || n_steps <= 0)
+        return fail(AXQ8_ERR_INVALID, "axdec_decode_continue: bad argument");
+    if (m->sess_pos < 0 || n_seq != m->sess_seq)
+        return fail(AXQ8_ERR_STATE,
+                    "axdec_decode_continue: no session of %d sequences (call axdec_prefill)", n_seq);
+    if (m->sess_pos + n_steps > m->c.max_ctx)
+        return fail(AXQ8_ERR_INVALID, "axdec_decode_continue: %d steps from position %d exceed max_ctx %d",
+                    n_steps, m->sess_pos, m->c.max_ctx);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    cudaGraphExec_t g;
+    int rc = get_graph(m, n_seq, &g);
+    if (rc) return rc;
+    if (first_tokens)
+        AXQ8_CUDA_TRY(cudaMemcpyAsync(m->tokens, first_tokens, sizeof(int) * n_seq,
+                                      cudaMemcpyHostToDevice, s),
+                      "axdec_decode_continue: tokens upload");
+    // record the greedy tokens of positions sess_pos + 1 .. (out_tokens rows of n_steps)
+    const int ctl[3] = {m->sess_pos + 1, 0, n_steps};
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->ctl, ctl, sizeof(ctl), cudaMemcpyHostToDevice, s),
+                  "axdec_decode_continue: ctl upload");
+    cudaEvent_t e0 = nullptr, e1 = nullptr;
+    if (decode_ms) {
+        AXQ8_CUDA_TRY(cudaEventCreate(&e0), "event");
+        AXQ8_CUDA_TRY(cudaEventCreate(&e1), "event");
+        cudaEventRecord(e0, s);
+    }
+    for (int r = 0; r < n_steps; r++) AXQ8_CUDA_TRY(cudaGraphLaunch(g, s), "axdec: graph launch");
+    if (decode_ms) cudaEventRecord(e1, s);
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(out_tokens, m->out_tokens, sizeof(int) * (size_t)n_seq * n_steps,
+                                  cudaMemcpyDeviceToHost, s),
+                  "axdec_decode_continue: tokens copy");
+    const int ctl0[3] = {0, 0, 0};
+    AXQ8_CUDA_TRY(cudaMemcpyAsync(m->ctl, ctl0, sizeof(ctl0), cudaMemcpyHostToDevice, s),
+                  "axdec_decode_continue: ctl reset");
+    AXQ8_CUDA_TRY(cudaStreamSynchronize(s), "axdec_decode_continue");
+    if (decode_ms) {
+        cudaEventElapsedTime(decode_ms, e0, e1);
+        cudaEventDestroy(e0);
+        cudaEventDestroy(e1);
+    }
+    m->sess_pos += n_steps;
     return AXQ8_OK;
 }
 

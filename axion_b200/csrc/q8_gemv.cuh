@@ -123,7 +123,7 @@ __device__ inline float dot16_f32(const int4 w, const float* __restrict__ xa) {
     float s = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; i++) {
-        const float4 v = __ldg(x4 + i);
+        const float4 v = __ldcg(x4 + i);
         const int q = ws[i];
         s = fmaf(v.x, (float)(int8_t)(q & 0xff), s);
         s = fmaf(v.y, (float)(int8_t)((q >> 8) & 0xff), s);
@@ -193,8 +193,7 @@ __device__ __forceinline__ void pair_load(PairLoad& L, const uint8_t* ra, const 
 // partials with one shuffle, so each block dot is exact before it is scaled.
 template <int MT, bool A32>
 __device__ __forceinline__ void pair_compute(const PairLoad& L, const GemvArgs& a,
-                                             const int8_t* __restrict__ xq,
-                                             const float* __restrict__ dx, int base, int cend,
+                                             const int8_t* xq, const float* dx, int base, int cend,
                                              int m0, int lane, float (&acc)[2][MT]) {
     const int K = (int)a.K;
     const int nb = K / QK;
@@ -257,7 +256,7 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, int m, int64_t n, bo
     if (EPI == EPI_ROPE_KV) {
         const int hd = a.hd, half = hd / 2, B = a.kv_block;
         const int64_t Nq = (int64_t)a.n_heads * hd, Nkv = (int64_t)a.n_kv * hd;
-        const int p = a.pos[m];
+        const int p = ld_cg(a.pos + m);
         if (p < 0 || p >= a.max_ctx) {
             record_status(a.status, AXQ8_ERR_INVALID);
             return;
@@ -298,7 +297,7 @@ __device__ __forceinline__ void epi_pair(const GemvArgs& a, int m, int64_t n, bo
     for (int r = 0; r < 2; r++) {
         if (r == 1 && !has_b) break;
         float v = r ? v1 : v0;
-        if (a.residual) v += a.residual[(int64_t)m * a.ldy + n + r];
+        if (a.residual) v += ld_cg(a.residual + (int64_t)m * a.ldy + n + r);
         a.y[(int64_t)m * a.ldy + n + r] = v;
         if (EPI == EPI_ARGMAX) atomicMax(keys + m, argmax_key(v, (int)(n + r) + a.idx_offset));
     }
@@ -417,16 +416,16 @@ __device__ __forceinline__ void argmax_tail(const GemvArgs& a, const unsigned lo
         return;
     }
     if (threadIdx.x == 0) {
-        const int n_prompt = a.ctl[0], feed_len = a.ctl[1], max_out = a.ctl[2];
+        const int n_prompt = ld_cg(a.ctl), feed_len = ld_cg(a.ctl + 1), max_out = ld_cg(a.ctl + 2);
         for (int m = 0; m < a.M; m++) {
             const unsigned long long k = atomicExch(a.amax_key + m, 0ull);
             const int idx = k == 0ull ? 0 : argmax_key_index(k);
-            const int p = a.pos[m];
+            const int p = ld_cg(a.pos + m);
             const int np = p + 1;
             a.argmax_out[m] = idx;
             if (np >= n_prompt && np - n_prompt < max_out)
                 a.out_tokens[m * max_out + (np - n_prompt)] = idx;
-            a.tokens[m] = np < feed_len ? a.feed[m * feed_len + np] : idx;
+            a.tokens[m] = np < feed_len ? ld_cg(a.feed + m * feed_len + np) : idx;
             a.pos[m] = np;
         }
         *a.done = 0;
@@ -484,9 +483,9 @@ __global__ void __launch_bounds__(kGemvWarps * 32, kGemvCtasPerSm) q8_gemv_kerne
         if (PRO == PRO_Q8 && a.act_smem > 0) {
             const int qbytes = a.M * K;
             for (int o = threadIdx.x * 16; o < qbytes; o += kGemvWarps * 32 * 16)
-                *reinterpret_cast<int4*>(act_q + o) = __ldg(reinterpret_cast<const int4*>(a.xq + o));
+                *reinterpret_cast<int4*>(act_q + o) = __ldcg(reinterpret_cast<const int4*>(a.xq + o));
             const int nd = a.M * (K / QK);
-            for (int o = threadIdx.x; o < nd; o += kGemvWarps * 32) act_d[o] = __ldg(a.dx + o);
+            for (int o = threadIdx.x; o < nd; o += kGemvWarps * 32) act_d[o] = __ldcg(a.dx + o);
             __syncthreads();
             xq = act_q;
             dx = act_d;

@@ -74,7 +74,7 @@ __global__ void quantize_act_kernel(const float* __restrict__ x, int64_t nblocks
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t blk = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5);
          blk < nblocks; blk += warps) {
-        const float v = x[blk * QK + lane];
+        const float v = ld_cg(x + blk * QK + lane);
         const uint32_t abits = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
         const float amax = __uint_as_float(abits);
         const float d = __fdiv_rn(amax, 127.0f);
@@ -408,8 +408,8 @@ int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int
         // tensor-core paths: xq [M][K] + transposed scales dxT [K/32][Mp]
         const size_t q_bytes = ((size_t)M * w->K + 255) / 256 * 256;
         const size_t d_bytes = sizeof(float) * (size_t)nb * mma_scale_pitch(M);
-        uint8_t* ws = static_cast<uint8_t*>(workspace(ds, q_bytes + d_bytes));
-        if (!ws) return AXQ8_ERR_ALLOC;
+        uint8_t* ws = static_cast<uint8_t*>(workspace(ds, q_bytes + d_bytes, s));
+        if (!ws) return capture_active(s) ? AXQ8_ERR_STATE : AXQ8_ERR_ALLOC;
         int8_t* xq = reinterpret_cast<int8_t*>(ws);
         float* dxT = reinterpret_cast<float*>(ws + q_bytes);
         if ((rc = mma_quantize(ds, x, M, w->K, xq, dxT, s))) return rc;
@@ -417,8 +417,8 @@ int axq8_linear(const axq8_weight_t* w, const float* x, int64_t M, float* y, int
         return mma_linear(ds, w, xq, dxT, M, nullptr, y, w->N, nullptr, s);
     }
     const size_t q_bytes = ((size_t)M * w->K + 255) / 256 * 256;
-    uint8_t* ws = static_cast<uint8_t*>(workspace(ds, q_bytes + (size_t)M * nb * sizeof(float)));
-    if (!ws) return AXQ8_ERR_ALLOC;
+    uint8_t* ws = static_cast<uint8_t*>(workspace(ds, q_bytes + (size_t)M * nb * sizeof(float), s));
+    if (!ws) return capture_active(s) ? AXQ8_ERR_STATE : AXQ8_ERR_ALLOC;
     int8_t* xq = reinterpret_cast<int8_t*>(ws);
     float* dx = reinterpret_cast<float*>(ws + q_bytes);
     rc = axq8_quantize_act(x, M, w->K, xq, dx, stream);
@@ -450,8 +450,8 @@ int axq8_quantize_weight_tensor(const float* w, int64_t K, int64_t N, int8_t* q,
     DeviceState* ds = device_state();
     if (!ds) return AXQ8_ERR_CUDA;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    unsigned* amax = static_cast<unsigned*>(workspace(ds, 256));
-    if (!amax) return AXQ8_ERR_ALLOC;
+    unsigned* amax = static_cast<unsigned*>(workspace(ds, 256, s));
+    if (!amax) return capture_active(s) ? AXQ8_ERR_STATE : AXQ8_ERR_ALLOC;
     AXQ8_CUDA_TRY(cudaMemsetAsync(amax, 0, sizeof(unsigned), s), "memset amax");
     const int64_t n = K * N;
     absmax_kernel<<<grid_for(ds, n, 256), 256, 0, s>>>(w, n, amax);

@@ -66,10 +66,16 @@ constexpr int kCounterSlots = 1 << 16;
 SplitScratch g_split[kMaxDevices];
 std::mutex g_split_mu;
 
-int split_scratch(DeviceState* ds, size_t part_bytes, float** part, int** counters) {
+int split_scratch(DeviceState* ds, size_t part_bytes, float** part, int** counters,
+                  cudaStream_t stream) {
     std::lock_guard<std::mutex> lk(g_split_mu);
     if (ds->device < 0 || ds->device >= kMaxDevices) return fail(AXQ8_ERR_INVALID, "device id");
     SplitScratch& sc = g_split[ds->device];
+    if ((!sc.counters || sc.part_bytes < part_bytes) && capture_active(stream))
+        return fail(AXQ8_ERR_STATE,
+                    "split-K scratch must grow to %zu bytes during a stream capture; make a call "
+                    "of this size outside capture first (or pass caller-owned scratch)",
+                    part_bytes);
     if (!sc.counters) {
         AXQ8_CUDA_TRY(cudaMalloc(&sc.counters, sizeof(int) * kCounterSlots), "split counters");
         AXQ8_CUDA_TRY(cudaMemset(sc.counters, 0, sizeof(int) * kCounterSlots), "split counters");
@@ -198,7 +204,7 @@ int mma_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const 
         } else {
             if (tiles > kCounterSlots)
                 return fail(AXQ8_ERR_UNSUPPORTED, "tensor-core linear: too many split tiles");
-            rc = split_scratch(ds, need, &a.part, &a.counters);
+            rc = split_scratch(ds, need, &a.part, &a.counters, stream);
             if (rc) return rc;
         }
     }

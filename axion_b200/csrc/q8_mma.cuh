@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
                     if (m < a.M) {
                         const float v = (j & 1) ? acc[j / 2].y : acc[j / 2].x;
                         const int64_t o = (int64_t)m * a.ldy + n;
-                        a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+                        a.y[o] = a.residual ? __fadd_rn(ld_cg(a.residual + o), v) : v;
                     }
                 }
             }
@@ -434,7 +434,7 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
                     for (int j = 0; j < 16; j++) {
                         if (mb + j >= a.M) break;
                         const int64_t o = (int64_t)(mb + j) * a.ldy + n;
-                        a.y[o] = a.residual ? __fadd_rn(a.residual[o], v[j]) : v[j];
+                        a.y[o] = a.residual ? __fadd_rn(ld_cg(a.residual + o), v[j]) : v[j];
                     }
                 }
             }
@@ -461,7 +461,7 @@ __global__ void quantize_act_t_kernel(const float* __restrict__ x, int M, int K,
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     for (int64_t blk = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); blk < nblocks;
          blk += warps) {
-        const float v = x[blk * QK + lane];
+        const float v = ld_cg(x + blk * QK + lane);
         const uint32_t abits = __reduce_max_sync(0xffffffffu, __float_as_uint(fabsf(v)));
         const float amax = __uint_as_float(abits);
         const float d = __fdiv_rn(amax, 127.0f);
@@ -483,7 +483,7 @@ __global__ void transpose_scales_kernel(const float* __restrict__ dx, int M, int
     for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < total;
          i += (int64_t)gridDim.x * blockDim.x) {
         const int m = (int)(i / nb), b = (int)(i % nb);
-        dxT[(int64_t)b * Mp + m] = dx[i];
+        dxT[(int64_t)b * Mp + m] = ld_cg(dx + i);
     }
 }
 

@@ -221,7 +221,7 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
                 if (n >= a.N || m >= a.M) continue;
                 const int64_t o = (int64_t)m * a.ldy + n;
                 const float v = (e & 1) ? acc[j][e >> 1].y : acc[j][e >> 1].x;
-                a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+                a.y[o] = a.residual ? __fadd_rn(ld_cg(a.residual + o), v) : v;
             }
         return;
     }
@@ -259,7 +259,7 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
         const int n = nb0 + r;
         if (n < a.N) {
             const int64_t o = (int64_t)m * a.ldy + n;
-            a.y[o] = a.residual ? __fadd_rn(a.residual[o], v) : v;
+            a.y[o] = a.residual ? __fadd_rn(ld_cg(a.residual + o), v) : v;
         }
     }
     cluster.sync();   // peers' tiles stay alive until every slice is read

@@ -72,9 +72,28 @@ DeviceState* device_state() {
     return ds;
 }
 
-void* workspace(DeviceState* ds, size_t bytes) {
+bool capture_active(cudaStream_t stream) {
+    cudaStreamCaptureStatus st = cudaStreamCaptureStatusNone;
+    const cudaError_t e = cudaStreamIsCapturing(stream, &st);
+    if (e != cudaSuccess) {
+        (void)cudaGetLastError();   // e.g. the legacy stream queried during a global capture
+        return true;
+    }
+    return st != cudaStreamCaptureStatusNone;
+}
+
+void* workspace(DeviceState* ds, size_t bytes, cudaStream_t stream) {
     std::lock_guard<std::mutex> lk(g_mu);
     if (ds->workspace_bytes >= bytes) return ds->workspace;
+    if (capture_active(stream)) {
+        // a grow synchronizes the device and frees the old buffer, neither of
+        // which a stream capture allows
+        fail(AXQ8_ERR_STATE,
+             "workspace must grow to %zu bytes during a stream capture; make a call of this "
+             "size outside capture first",
+             bytes);
+        return nullptr;
+    }
     if (ds->workspace) {
         cudaDeviceSynchronize();   // the old buffer may still be read by queued kernels
         cudaFree(ds->workspace);

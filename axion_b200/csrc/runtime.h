@@ -34,8 +34,13 @@ struct DeviceState {
 DeviceState* device_state();
 
 // Grow-only per-device workspace for quantized activations and partials.
-// Synchronizes the device before replacing a smaller buffer.
-void* workspace(DeviceState* ds, size_t bytes);
+// Synchronizes the device before replacing a smaller buffer; returns nullptr
+// (AXQ8_ERR_STATE recorded) when a grow is needed while `stream` is captured.
+void* workspace(DeviceState* ds, size_t bytes, cudaStream_t stream);
+
+// Whether `stream` is being captured into a CUDA graph (an error from the
+// query counts as capturing: nothing that needs a synchronization may run).
+bool capture_active(cudaStream_t stream);
 
 // Synthetic Q8_0 weight slice in the repacked row layout: rows [row0,
 // row0 + N) and columns [col0, col0 + K) of the [*, Kfull] tensor that

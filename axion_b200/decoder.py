@@ -155,6 +155,57 @@ class Decoder:
             C.c_void_p(stream) if stream else None))
         return out, lg, ms.value
 
+    def set_prefill(self, batched: bool) -> None:
+        """Batched prefill of prompts (default, where supported) or one
+        position at a time through the decode step."""
+        check(self.lib.axdec_set_prefill(self.h, 1 if batched else 0))
+
+    def prefill_batched(self, n_seq: int) -> bool:
+        return bool(self.lib.axdec_prefill_batched(self.h, n_seq))
+
+    def prefill(self, tokens, stream=None) -> None:
+        """Start a step-wise session: tokens [n_seq, n_tok] fill the KV cache
+        at positions 0 .. n_tok - 1 (StreamingExecutor::begin_decode plus the
+        prompt); decode_step continues at position n_tok."""
+        t = np.ascontiguousarray(np.atleast_2d(np.asarray(tokens, np.int32)))
+        n_seq, n_tok = t.shape
+        check(self.lib.axdec_prefill(self.h, t.ctypes.data_as(C.c_void_p), n_seq, n_tok,
+                                     C.c_void_p(stream) if stream else None))
+
+    def decode_step(self, tokens, logits: bool = False, stream=None):
+        """One decode position for every sequence of the session
+        (StreamingExecutor::decode_step): input token per sequence in, greedy
+        next token per sequence out (and the step's logits [n_seq, vocab])."""
+        t = np.ascontiguousarray(np.asarray(tokens, np.int32).reshape(-1))
+        nxt = np.empty_like(t)
+        lg = np.empty((t.size, self.cfg.vocab_local), np.float32) if logits else None
+        check(self.lib.axdec_decode_step(self.h, t.ctypes.data_as(C.c_void_p), t.size,
+                                         nxt.ctypes.data_as(C.c_void_p),
+                                         lg.ctypes.data_as(C.c_void_p) if lg is not None else None,
+                                         C.c_void_p(stream) if stream else None))
+        return (nxt, lg) if logits else nxt
+
+    def decode_step_ptr(self, tokens_ptr: int, n_seq: int, next_ptr: int, stream=None) -> None:
+        """decode_step on caller-owned host buffers (e.g. pinned memory)."""
+        check(self.lib.axdec_decode_step(self.h, C.c_void_p(tokens_ptr), n_seq,
+                                         C.c_void_p(next_ptr), None,
+                                         C.c_void_p(stream) if stream else None))
+
+    def decode_continue(self, n_steps: int, n_seq: int, first=None, stream=None):
+        """n_steps greedy steps of the session on the device, tokens fed back
+        on the device; returns (tokens [n_seq, n_steps], device ms)."""
+        out = np.empty((n_seq, n_steps), np.int32)
+        f = None
+        if first is not None:
+            f = np.ascontiguousarray(np.asarray(first, np.int32).reshape(-1))
+            assert f.size == n_seq
+        ms = C.c_float(0)
+        check(self.lib.axdec_decode_continue(self.h, f.ctypes.data_as(C.c_void_p) if f is not None
+                                             else None, n_seq, n_steps,
+                                             out.ctypes.data_as(C.c_void_p), C.byref(ms),
+                                             C.c_void_p(stream) if stream else None))
+        return out, ms.value
+
     def forced(self, tokens, n_prompt: int, stream=None) -> np.ndarray:
         """Teacher-forced logits [n_steps - n_prompt + 1, n_seq, vocab] (this
         rank's vocabulary slice under tensor parallelism)."""
@@ -165,6 +216,26 @@ class Decoder:
                                     n_steps, lg.ctypes.data_as(C.c_void_p),
                                     C.c_void_p(stream) if stream else None))
         return lg
+
+
+_SLOTS = ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
+          "ffn_up", "ffn_down")
+
+
+def tensor_index(n_layers: int, name: str) -> int:
+    """axdec_tensor_index without the library: token_embd 0, output 1,
+    output_norm 2, then 3 + 9 * layer + slot (the per-tensor seed offset of
+    axdec_init_random), -1 for an unknown name."""
+    fixed = {"token_embd.weight": 0, "output.weight": 1, "output_norm.weight": 2}
+    if name in fixed:
+        return fixed[name]
+    parts = name.split(".")
+    if len(parts) != 4 or parts[0] != "blk" or parts[3] != "weight" or not parts[1].isdigit():
+        return -1
+    layer = int(parts[1])
+    if layer >= n_layers or parts[2] not in _SLOTS:
+        return -1
+    return 3 + 9 * layer + _SLOTS.index(parts[2])
 
 
 def share_tp_id(rank: int, make_id, group=None) -> bytes:

@@ -79,8 +79,11 @@ int axdec_tensor_index(const axdec_config_t* cfg, const char* name);
 
 /* Greedy generation for n_seq sequences (<= max_batch) sharing one prompt
  * length: prompts[n_seq, n_prompt] (host), then n_new greedy tokens written
- * to out_tokens[n_seq, n_new] (host).  The prompt is fed one position at a
- * time through the decode step, as ModelRunner::generate does.  When
+ * to out_tokens[n_seq, n_new] (host).  Prompt positions 0 .. n_prompt - 2 run
+ * as a batched prefill where axdec_prefill_batched says so (A8, fp16 pages,
+ * head dim 64 / 128), else one position at a time through the decode step, as
+ * ModelRunner::generate does (model_runner.cpp:291-295); the last prompt
+ * position always goes through the decode step and yields the first token.  When
  * logits_out is non-null it receives the LM-head logits of every generated
  * step [n_new, n_seq, vocab] (host; slows the loop: one copy per step).
  * The decode step runs as a CUDA graph on `stream`.  On return *decode_ms
@@ -94,6 +97,44 @@ int axdec_generate(axdec_model_t* m, const int32_t* prompts, int32_t n_seq, int3
  * the logits of the next token: logits_out[n_steps - n_prompt + 1, n_seq, vocab]. */
 int axdec_forced(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t n_prompt,
                  int32_t n_steps, float* logits_out, void* stream);
+
+/* Batched prefill: prompt positions as wide products (rows = sequences x
+ * positions, in chunks of up to 4096 rows: the tcgen05 product above 64 rows,
+ * the skinny one up to 64) and a causal GQA attention kernel over the paged
+ * cache — StreamingExecutor::execute_layer (streaming_executor.cpp:110-238)
+ * with mha_attention (mha.cpp:167-198) for a whole prompt.  mode 1 (default):
+ * used wherever supported; mode 0: prompts go through the decode step one
+ * position at a time.  axdec_prefill_batched tells whether prompts of n_seq
+ * sequences take it.  The chunk buffers are allocated on the first batched
+ * prefill and kept. */
+int axdec_set_prefill(axdec_model_t* m, int mode);
+int axdec_prefill_batched(const axdec_model_t* m, int32_t n_seq);
+
+/* Step-wise decoding, StreamingExecutor::begin_decode + decode_step
+ * (streaming_executor.hpp:58-67, .cpp:244-253, 403-420) for a batch.
+ * axdec_prefill starts a session of n_seq sequences: tokens[n_seq, n_tok]
+ * (host) fill the KV cache at positions 0 .. n_tok - 1 (no logits; n_tok may
+ * be 0) and the session continues at position n_tok.  axdec_decode_step then
+ * takes one input token per sequence (host tokens[n_seq]), runs one decode
+ * step (the step's CUDA graph) at the session position, and writes the greedy
+ * next token of each sequence to next_tokens[n_seq] (host); logits_out
+ * (nullable, host) receives the step's logits [n_seq, vocab] (this rank's
+ * vocabulary slice under tensor parallelism).  Synchronous: each call returns
+ * when its outputs are in host memory.  axdec_generate and axdec_forced end
+ * the session (AXQ8_ERR_STATE from axdec_decode_step until the next
+ * axdec_prefill). */
+int axdec_prefill(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t n_tok,
+                  void* stream);
+int axdec_decode_step(axdec_model_t* m, const int32_t* tokens, int32_t n_seq, int32_t* next_tokens,
+                      float* logits_out, void* stream);
+
+/* Continue the session for n_steps greedy steps on the device (each step's
+ * token fed back without a host round trip): the first step's inputs are
+ * first_tokens[n_seq] (host), or, when null, the greedy tokens of the
+ * session's previous step.  out_tokens[n_seq, n_steps] (host) receives the
+ * tokens; *decode_ms (nullable) the device time of the n_steps steps. */
+int axdec_decode_continue(axdec_model_t* m, const int32_t* first_tokens, int32_t n_seq,
+                          int32_t n_steps, int32_t* out_tokens, float* decode_ms, void* stream);
 
 /* Bytes of device memory the model holds (weights + KV pages + buffers). */
 int64_t axdec_device_bytes(const axdec_model_t* m);

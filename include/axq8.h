@@ -141,12 +141,16 @@ int axq8_linear_q8act(const axq8_weight_t* w, const int8_t* xq, const float* dx,
  * owns all of HBM) or code that must not risk the device synchronization
  * cudaMalloc/cudaFree can cause.  No counterpart in the reference (its
  * linear runs on the host).  Allocates nothing: the quantized activation
- * goes to a fixed 1.125 MiB static device array that every GPU loading this
+ * goes to a fixed 1.1875 MiB static device array that every GPU loading this
  * library reserves until exit.  Limit: M*K <= 1,048,576, else
- * AXQ8_ERR_INVALID.  The array is shared by all calls on a device: calls
- * that overlap on the GPU race and must be serialized by the caller.  The
- * first call on a device looks up the array's address; make it before any
- * stream capture. */
+ * AXQ8_ERR_INVALID.  Kernels: the GEMV for M <= 8 and M > 64, the skinny
+ * product for 8 < M <= 64 (both as axq8_linear picks them); above 64 rows
+ * axq8_linear's tcgen05 product needs split-K scratch, so this entry point
+ * stays on the GEMV there (slower; same values up to fp32 combination
+ * order).  The array is shared by all calls on a device: calls that overlap
+ * on the GPU race and must be serialized by the caller.  The first call on a
+ * device looks up the array's address and keeps it; make it before any
+ * stream capture, and do not use the library across a cudaDeviceReset. */
 int axq8_linear_noalloc(const axq8_weight_t* w, const float* x, int64_t M, float* y,
                         void* stream);
 

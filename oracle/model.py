@@ -90,8 +90,10 @@ class OracleLlama:
         row = blocks[tok * (H // QK) * Q8_0_BYTES:(tok + 1) * (H // QK) * Q8_0_BYTES]
         return self.o.dequant(row, H)
 
-    def decode(self, prompt, n_new: int, act: str = "f32", kv: str = "f32"):
-        """Greedy incremental decode; returns (logits [n_new, vocab], new tokens)."""
+    def decode(self, prompt, n_new: int, act: str = "f32", kv: str = "f32", forced=None):
+        """Greedy incremental decode; returns (logits [n_new, vocab], new tokens).
+        With `forced` (n_new - 1 tokens) step s + 1 is fed forced[s] instead of
+        the argmax of step s (teacher forcing); the argmaxes are still returned."""
         c = self.cfg
         o = self.o
         kc = [np.zeros((0, c.n_kv_heads * c.head_dim), np.float32) for _ in range(c.n_layers)]
@@ -136,5 +138,5 @@ class OracleLlama:
             nxt = o.argmax(lg)
             toks.append(nxt)
             if s + 1 < n_new:
-                last = step(self.embed(nxt))
+                last = step(self.embed(int(forced[s]) if forced is not None else nxt))
         return logits, toks

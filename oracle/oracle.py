@@ -9,6 +9,8 @@ implementation (see q8_oracle.h / ref_shim.cpp).
 from __future__ import annotations
 
 import ctypes as C
+import os
+import re
 import subprocess
 from pathlib import Path
 
@@ -18,7 +20,25 @@ HERE = Path(__file__).resolve().parent
 ORACLE_SO = HERE / "liboracle.so"
 REF_SO = HERE / "_ref" / "libaxion_ref.so"
 REF_VALIDATION = HERE / "_ref" / "axion_runtime_validation"
-REF_SRC = Path("/root/reference/inference/cpp")
+
+
+def _ref_src() -> Path:
+    """The reference's inference/cpp source tree: $AXION_REF_SRC, else the
+    `REF ?=` default of the Makefile that builds the reference library (one
+    place names the location; `make REF=...` and this variable override it)."""
+    env = os.environ.get("AXION_REF_SRC")
+    if env:
+        return Path(env)
+    try:
+        m = re.search(r"^REF\s*\?=\s*(\S+)", (HERE / "Makefile").read_text(), re.M)
+        if m:
+            return Path(m.group(1))
+    except OSError:
+        pass
+    return HERE / "_ref" / "src-not-configured"
+
+
+REF_SRC = _ref_src()
 
 QK = 32
 Q8_0_BYTES = 34
@@ -37,7 +57,7 @@ def build(ref: bool | None = None) -> None:
         ref = REF_SRC.exists()
     if ref:
         targets.append("ref")
-    subprocess.run(["make", "-s", "-C", str(HERE), *targets], check=True)
+    subprocess.run(["make", "-s", "-C", str(HERE), f"REF={REF_SRC}", *targets], check=True)
 
 
 class Oracle:

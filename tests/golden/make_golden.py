@@ -26,6 +26,16 @@ oracle/Makefile) called through oracle/ref_shim.cpp:
                             linears (written by axion_b200.gguf.GGUFWriter)
 * tiny_llama_ref.npz        ModelRunner::generate greedy tokens and the
                             per-step logits of the same incremental decode
+* tinyllama_width_256.npz   256 greedy steps of ModelRunner::generate (and the
+                            per-step logits) on a 2-layer model of TinyLlama's
+                            layer widths (hidden 2048, FFN 5632, 32/4 heads of
+                            64) with a 2048-token vocabulary, whose Q8_0
+                            weights are the device generator's
+                            (axq8_synth_q8_0 seed + tensor index, std 0.02;
+                            norms 1.0), so the GPU test rebuilds the same model
+                            with axdec_init_random instead of reading a file.
+                            `python tests/golden/make_golden.py --long` writes
+                            it alone (about two minutes of host time).
 """
 from __future__ import annotations
 
@@ -99,6 +109,74 @@ def write_tiny_llama(o: Oracle, path: Path, seed: int = SEED) -> dict:
     q8("output.weight", V, H, std=0.2)
     g.write(path)
     return c
+
+
+# 256-step greedy fixture: TinyLlama layer widths, 2 layers, small vocabulary
+LONG = dict(n_layers=2, hidden=2048, n_heads=32, n_kv_heads=4, head_dim=64, ffn=5632, vocab=2048,
+            rope_theta=10000.0, rms_eps=1e-5)
+LONG_SEED = 0x256
+LONG_PROMPT_LEN = 16
+LONG_NEW = 256
+
+
+def long_index(name: str) -> int:
+    from axion_b200.decoder import tensor_index
+    return tensor_index(LONG["n_layers"], name)
+
+
+def write_long_model(o: Oracle, path: Path) -> None:
+    c = LONG
+    H, F, V = c["hidden"], c["ffn"], c["vocab"]
+    hq, hkv = c["n_heads"] * c["head_dim"], c["n_kv_heads"] * c["head_dim"]
+    g = GGUFWriter()
+    g.add_string("general.architecture", "llama")
+    for k, v in [("block_count", c["n_layers"]), ("attention.head_count", c["n_heads"]),
+                 ("attention.head_count_kv", c["n_kv_heads"]), ("embedding_length", H),
+                 ("feed_forward_length", F), ("rope.dimension_count", c["head_dim"]),
+                 ("vocab_size", V)]:
+        g.add_u32(f"llama.{k}", v)
+    g.add_f32("llama.rope.freq_base", c["rope_theta"])
+    g.add_f32("llama.attention.layer_norm_rms_epsilon", c["rms_eps"])
+
+    def q8(name, N, K):
+        g.add_tensor(name, o.synth_q8_0(LONG_SEED + long_index(name), N, K, 0.02), (N, K), Q8_0)
+
+    ones = np.ones(H, np.float32)
+    q8("token_embd.weight", V, H)
+    for i in range(c["n_layers"]):
+        p = f"blk.{i}."
+        g.add_tensor(p + "attn_norm.weight", ones, (H,), F32)
+        q8(p + "attn_q.weight", hq, H)
+        q8(p + "attn_k.weight", hkv, H)
+        q8(p + "attn_v.weight", hkv, H)
+        q8(p + "attn_output.weight", H, hq)
+        g.add_tensor(p + "ffn_norm.weight", ones, (H,), F32)
+        q8(p + "ffn_gate.weight", F, H)
+        q8(p + "ffn_up.weight", F, H)
+        q8(p + "ffn_down.weight", H, F)
+    g.add_tensor("output_norm.weight", ones, (H,), F32)
+    q8("output.weight", V, H)
+    g.write(path)
+
+
+def make_long(o: Oracle, r: RefLib) -> None:
+    path = HERE / "_long.gguf"
+    write_long_model(o, path)
+    prompt = np.random.default_rng(LONG_SEED).integers(0, LONG["vocab"], LONG_PROMPT_LEN)
+    prompt = prompt.astype(np.int32)
+    toks = r.generate(path, prompt, LONG_NEW)
+    logits, am = r.decode_logits(path, prompt, LONG_NEW, LONG["vocab"])
+    path.unlink()
+    assert toks[LONG_PROMPT_LEN:] == am.tolist(), "generate and the per-step decode disagree"
+    srt = np.sort(logits, axis=1)
+    margin = (srt[:, -1] - srt[:, -2]) / np.max(np.abs(logits), axis=1)
+    np.savez_compressed(HERE / "tinyllama_width_256.npz", prompt=prompt,
+                        tokens=np.array(toks[LONG_PROMPT_LEN:], np.int32), logits=logits,
+                        seed=np.int64(LONG_SEED), min_margin=np.float32(margin.min()),
+                        config=np.array([LONG[k] for k in ("n_layers", "hidden", "n_heads",
+                                                           "n_kv_heads", "head_dim", "ffn",
+                                                           "vocab")], np.int64))
+    print("long run: smallest top-2 margin (relative)", float(margin.min()))
 
 
 def main() -> None:
@@ -181,4 +259,8 @@ def main() -> None:
 
 
 if __name__ == "__main__":
-    main()
+    if "--long" in sys.argv:
+        make_long(Oracle(), RefLib())
+    else:
+        main()
+        make_long(Oracle(), RefLib())

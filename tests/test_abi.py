@@ -109,3 +109,21 @@ def test_tensor_core_entry_points_validate_shapes():
     assert rc == _lib.AXQ8_ERR_UNSUPPORTED and b"M <= 64" in lib.axq8_last_error()
     assert lib.axq8_linear_path(ctypes.byref(w), 64, _lib.AXQ8_ACT_F32) == _lib.AXQ8_PATH_GEMV
     assert lib.axq8_quantize_act_t(None, 4, 33, None, None, None) == _lib.AXQ8_ERR_INVALID
+
+
+def test_tensor_index_matches_library():
+    """The library-free axdec_tensor_index twin (used by the reference arm of
+    the benchmark, which must not load libaxq8.so) agrees on every name."""
+    import ctypes as C
+    from axion_b200 import _lib
+    from axion_b200.decoder import DecoderConfig, tensor_index
+    lib = _lib.load()
+    cc = DecoderConfig(n_layers=5, hidden=64, ffn=64, n_heads=2, n_kv_heads=1, head_dim=32,
+                       vocab=64).c()
+    names = ["token_embd.weight", "output.weight", "output_norm.weight", "blk.5.attn_q.weight",
+             "blk.0.bogus.weight", "blk.x.attn_q.weight", "nothing"]
+    names += [f"blk.{i}.{s}.weight" for i in range(5) for s in
+              ("attn_norm", "attn_q", "attn_k", "attn_v", "attn_output", "ffn_norm", "ffn_gate",
+               "ffn_up", "ffn_down")]
+    for n in names:
+        assert tensor_index(5, n) == lib.axdec_tensor_index(C.byref(cc), n.encode()), n

@@ -165,3 +165,34 @@ def test_dispatch_by_width(cuda, oracle):
     _, _, w2 = _case(oracle, 64, 256, 1, seed=0)
     assert ops.linear_path(w2, 256) == "gemv"        # N < 128
     assert ops.linear_path(w2, 40) == "skinny"       # any N
+
+
+# The prefill sweep's Llama-2-7B linear shapes at M = 256 and 2048: the
+# product through axq8_linear (A8, tcgen05 at these widths) on sampled output
+# rows against the oracle's A8 linear and the reference's fp32 arithmetic.
+SWEEP = [(4096, 4096), (11008, 4096), (4096, 11008), (32000, 4096)]
+
+
+@pytest.mark.parametrize("M", [256, 2048])
+@pytest.mark.parametrize("N,K", SWEEP)
+def test_prefill_sweep_shapes_vs_oracle(cuda, oracle, N, K, M):
+    ops = _ops()
+    blocks = oracle.synth_q8_0(0xA710 + N + K, N, K, 0.02)
+    w = ops.Q8Weight.from_blocks(blocks, N, K)
+    rng = np.random.default_rng(N + M)
+    x = rng.normal(0, 1, (M, K)).astype(np.float32)
+    assert ops.linear_path(w, M) == "tensor_core"
+    y = ops.linear_from_gguf(torch.from_numpy(x).cuda(), w).cpu().numpy()
+    rows = np.sort(rng.choice(M, 6, replace=False))
+    rows[0], rows[-1] = 0, M - 1             # first and last tile rows always
+    oq, od = oracle.quantize_act(x[rows])
+    ref = oracle.linear_a8(blocks, N, K, oq, od)
+    xd = _xdeq(oq, od)
+    wdeq = oracle.dequant(blocks, N * K).reshape(N, K)
+    scale = np.abs(xd.astype(np.float64)) @ np.abs(wdeq.astype(np.float64)).T
+    err = rel_err(y[rows], ref.astype(np.float64), scale)
+    print(f"sweep [{N}x{K}] M={M}: rows {rows.tolist()} err vs oracle {err:.2e}")
+    assert err <= A8_COMBINE_TOL
+    assert rel_err(y[rows], oracle.linear_f32(xd, wdeq).astype(np.float64), scale) <= REL_TOL
+    assert np.isfinite(y).all()
+    assert ops.status() == 0

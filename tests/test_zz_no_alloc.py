@@ -4,8 +4,9 @@ Callers that run under a fixed device-memory budget (an allocator owning all
 of HBM) or that must not trigger the device synchronization a cudaMalloc can
 cause use this entry point: its scratch is a fixed static device array, so it
 allocates nothing.  This test calls it through the C ABI and checks it
-against axq8_linear (A8 mode) on two calls in a row — the second call reuses
-the array the first call left behind — plus the size limit.
+against axq8_linear (A8 mode) and against the oracle's A8 linear on two calls
+in a row — the second call reuses the array the first call left behind — at
+widths that run the GEMV and the skinny product, plus the size limit.
 
 Kept in a file of its own, named to be collected last; it must pass run alone
 in a fresh process as well as after the other tests.
@@ -32,23 +33,33 @@ def _call_noalloc(lib, w, x: torch.Tensor, y: torch.Tensor) -> int:
                                    C.c_void_p(y.data_ptr()), s)
 
 
-def test_noalloc_matches_linear_two_calls(cuda, oracle):
+@pytest.mark.parametrize("N,K,Ms", [
+    (1500, 2048, (3, 1)),       # the GEMV, one and several 4-row passes
+    (1500, 4096, (16, 64)),     # the skinny product (axq8_linear's kernel at these widths)
+    (640, 4096, (80, 96)),      # above 64 rows: the GEMV here, tcgen05 in axq8_linear
+])
+def test_noalloc_matches_linear_two_calls(cuda, oracle, N, K, Ms):
     from axion_b200 import _lib, ops
     lib = _lib.load()
-    N, K = 1500, 2048
-    rng = np.random.default_rng(21)
+    rng = np.random.default_rng(21 + K + N)
     blocks = oracle.quantize_weight_blocks(rng.normal(0, 0.02, (N, K)).astype(np.float32))
     w = ops.Q8Weight.from_blocks(blocks, N, K)
     wd = w.dequantize().cpu().numpy().astype(np.float64)
     # two different inputs in a row: the second call must not see the first's data
-    for call, M in enumerate((3, 1)):
+    for call, M in enumerate(Ms):
         x = torch.from_numpy(rng.normal(0, 1, (M, K)).astype(np.float32)).cuda()
         y = torch.full((M, N), float("nan"), device="cuda")
         _lib.check(_call_noalloc(lib, w, x, y))
-        ref = ops.linear_from_gguf(x, w, act_mode="q8")
+        got = y.cpu().numpy()
         xn = x.cpu().numpy()
         scale = np.abs(xn.astype(np.float64)) @ np.abs(wd).T
-        assert rel_err(y.cpu().numpy(), ref.cpu().numpy().astype(np.float64), scale) <= REL_TOL, call
+        # against the existing entry point (axq8_linear, A8) ...
+        ref = ops.linear_from_gguf(x, w, act_mode="q8").cpu().numpy().astype(np.float64)
+        assert rel_err(got, ref, scale) <= REL_TOL, (call, M)
+        # ... and against the oracle's A8 linear on the same quantized input
+        xq, dx = oracle.quantize_act(xn)
+        want = oracle.linear_a8(blocks, N, K, xq, dx).astype(np.float64)
+        assert rel_err(got, want, scale) <= REL_TOL, (call, M)
     assert ops.status() == 0
 
 
