@@ -2,62 +2,55 @@
 """Benchmark of the B200 Q8_0 hot path; prints ONE JSON line (rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl axion|reference]
-                    [--workload decode|gemv|prefill|llama3|skinny]
+                    [--workload llama3|decode|gemv|prefill|skinny]
 
 Workloads
-  decode (default) TinyLlama-1.1B-architecture decode: 22
-         layers, hidden 2048, FFN 5632 SwiGLU, 32 query / 4 KV heads of 64,
-         vocab 32000, random-init Q8_0 weights (N(0, 0.02) before
-         quantization, generated on the device), batch 1, a random 128-token
-         prompt, then K (default 256) greedy decode steps over paged fp16 KV
-         (block 16).  One step = one decode token.  Metric: decode tokens/s
-         (device time of the K generation steps).  `e2e`: the same tokens over
-         the whole public axdec_generate call (host prompt in, host tokens
-         out, the 128 prompt positions included).  `roofline`: the step as a
-         weight stream (Q8_0 weights of all linears + LM head + KV read per
-         step) against the measured HBM bandwidth.  The reference arm runs
-         ModelRunner::generate on a GGUF holding the same weights.
-  gemv   Q8_0 GEMV, TinyLlama ffn_up shape: W [5632 x 2048] Q8_0 (random init,
-         N(0, 0.02) before quantization), x [1 x 2048] fp32 N(0, 1) quantized on
-         the fly, y [5632] fp32.  One step = one linear_from_gguf call.  The
-         weight rotates over enough copies (> 4 x L2) that every step streams
-         its weight from HBM.  Metric: algorithmic bytes / s (W 34/32 B per
-         weight + x + y = 12,285,952 B per step).
-  llama3 Llama-3-8B-architecture batched decode: 32
-         layers, hidden 4096, FFN 14336, 32/8 heads of 128, vocab 128256, RoPE
-         theta 5e5 (not given by the config; Llama-3's), batch 64, random
-         2048-token prompts, then K (default 128) greedy steps; tensor parallel
-         over the N GPUs of the run (strong scaling).  Every linear runs on the
-         skinny product at M = 64.  Metric: decode
-         tokens/s of the whole job; the reference arm is extrapolated from one
-         linear.
-  skinny the decode-width product (q8_mmq_kernel, mma.sync int8 with register
-         accumulators) on the Llama-3-8B layer shapes [6144x4096],
-         [4096x4096], [28672x4096], [4096x14336] at M = 16, 32, 64 with
-         pre-quantized activations.  One step = the 12 products.  Metric:
-         algorithmic bytes / s (weights once + activations + outputs); e2e runs
-         the public axq8_linear with host buffers.
-  prefill Q8_0 prefill GEMM sweep: Llama-2-7B linear
-         shapes [4096x4096], [11008x4096], [4096x11008], [32000x4096] x M in
-         {256, 1024, 2048, 4096} on the tcgen05 kind::i8 path.  One step = one
-         GEMM (cases in rotation; default K = 16 = the whole sweep).  Metric:
-         int8 TOPS (2*M*N*K / device time); roofline against the int8 dense
-         peak; the reference arm times linear_from_gguf on [4096x4096] for a
-         bounded M.
+  llama3 (default) Llama-3-8B-architecture batched decode: 32 layers, hidden
+         4096, FFN 14336 SwiGLU, 32 query / 8 KV heads of 128, vocab 128256,
+         RoPE theta 5e5 (Llama-3's), random-init Q8_0 weights (N(0, 0.02)
+         before quantization, generated on the device), 64 sequences with
+         random 2048-token prompts (batched prefill), then K (default 128)
+         greedy decode steps over paged fp16 KV (block 16), tensor parallel
+         over the N GPUs of the run (column-split Q/K/V/gate/up, row-split
+         O/down, vocabulary-split LM head, NCCL all-reduce; strong scaling).
+         One step = one decode position of all 64 sequences (64 tokens).
+         Metric: decode tokens/s of the whole job, device time of K steps
+         continued on the device (axdec_decode_continue).  `e2e`: the same
+         steps through the public step call (axdec_decode_step) with pinned
+         host token buffers, H2D of the 64 input tokens and D2H of the 64
+         next tokens inside every step.  `roofline`: the step as a weight +
+         KV stream per rank against the measured HBM bandwidth.
+  decode TinyLlama-1.1B-architecture decode: 22 layers, hidden 2048, FFN
+         5632, 32 query / 4 KV heads of 64, vocab 32000, batch 1, a random
+         128-token prompt, then K (default 256) greedy steps.  Metric: decode
+         tokens/s (device time of the K steps); `e2e`: the whole public
+         axdec_generate call (host prompt in, host tokens out, batched prefill
+         of the prompt included).
+  gemv   Q8_0 GEMV, TinyLlama ffn_up shape: W [5632 x 2048] Q8_0, x [1 x 2048]
+         fp32 N(0, 1) quantized on the fly, y [5632] fp32.  One step = one
+         linear_from_gguf call; the weight rotates over enough copies (> 4 x
+         L2) that every step streams it from HBM.  Metric: algorithmic bytes
+         / s (W 34/32 B per weight + x + y = 12,285,952 B per step).
+  skinny the decode-width product (q8_mmq_kernel) on the Llama-3-8B layer
+         shapes [6144x4096], [4096x4096], [28672x4096], [4096x14336] at M =
+         16, 32, 64 with pre-quantized activations.  One step = the 12
+         products.  Metric: algorithmic bytes / s.
+  prefill Q8_0 prefill GEMM sweep, Llama-2-7B linear shapes [4096x4096],
+         [11008x4096], [4096x11008], [32000x4096] x M in {256, 1024, 2048,
+         4096} on the tcgen05 kind::i8 path.  One step = one GEMM (cases in
+         rotation; default K = 16 = the whole sweep).  Metric: int8 TOPS.
 
 Arms
   --impl axion      the CUDA path (libaxq8.so) on N GPUs, one process per GPU
-                    (torchrun for N > 1; each rank runs its own replica: the
-                    GEMV does not shard, scaling "weak").
+                    (torchrun for N > 1).
   --impl reference  the reference's own CPU implementation (oracle/_ref,
-                    built from its sources) on the host cores, rank 0 only.
+                    built from its unmodified sources) on the host cores, rank
+                    0 only; each of the K steps is a bounded sample of the
+                    workload, and the line says how its rate follows from it.
+                    It loads no library of this repository.
 
 Timing: W untimed warm-up steps, then K steps between barrier +
 cudaDeviceSynchronize, CUDA events on the launching stream, max over ranks.
-`e2e` is the same metric through the public C-ABI entry point with host
-(pinned) buffers, H2D of x and D2H of y inside the timed region.
-`roofline` is the GEMV kernel alone (pre-quantized activation, CUDA events
-over back-to-back launches) against the measured HBM copy bandwidth.
 """
 from __future__ import annotations
 
@@ -355,10 +348,9 @@ def run_gemv_axion(args, d: Dist) -> dict:
         "ms_per_step": round(ms_max / steps_done, 6), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "int8 x int8 -> int32 -> fp32",
         "data": "synthetic (device-generated Q8_0 weights, N(0,0.02); x N(0,1))",
-        "config": {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K, "M": 1,
-                   "act": "q8", "l2_policy": f"rotating {n_copies} weight copies "
-                   f"({n_copies * wbytes / 2**20:.0f} MiB > 4 x L2)",
-                   "parallelism": f"replicas x{d.world}"},
+        "config": gemv_config(args, d.world),
+        "l2_policy": f"rotating {n_copies} weight copies ({n_copies * wbytes / 2**20:.0f} MiB > "
+                     f"4 x L2)",
         "e2e": {"value": round(e2e_val, 2), "unit": "GB/s",
                 "h2d_bytes_per_step": GEMV_K * 4, "d2h_bytes_per_step": GEMV_N * 4,
                 "steps": e2e_steps, "path": "axq8_linear (C ABI) + pinned H2D/D2H"},
@@ -395,7 +387,7 @@ def gemv_reference(args, steps: int) -> dict:
 # ---------------------------------------------------------------------------
 
 # ---------------------------------------------------------------------------
-# TinyLlama-architecture decode workload
+# TinyLlama-architecture decode workload (batch 1, 128-token prompt)
 # ---------------------------------------------------------------------------
 
 TL = dict(n_layers=22, hidden=2048, ffn=5632, n_heads=32, n_kv_heads=4, head_dim=64,
@@ -403,10 +395,14 @@ TL = dict(n_layers=22, hidden=2048, ffn=5632, n_heads=32, n_kv_heads=4, head_dim
 TL_PROMPT, TL_NEW, TL_SEED, TL_STD = 128, 256, 0xA710, 0.02
 DECODE_METRIC = "TinyLlama-arch Q8_0 decode tokens/s (batch 1, 128-token prompt, greedy)"
 DECODE_CONFIG = {"workload": "tinyllama_1.1b_arch_decode_q8_0", "layers": 22, "hidden": 2048,
-                 "ffn": 5632, "heads": "32q/4kv x 64", "vocab": 32000, "batch": 1,
-                 "prompt": TL_PROMPT, "new_tokens": TL_NEW, "kv": "paged fp16, block 16",
-                 "act": "q8 (A8W8 int8 block dots)",
+                 "ffn": 5632, "heads": "32q/4kv x 64", "vocab": 32000, "weights": "Q8_0",
+                 "batch": 1, "prompt": TL_PROMPT, "new_tokens": TL_NEW,
+                 "kv": "paged fp16, block 16",
                  "l2_policy": "weights 1.1 GB per step >> L2 (126 MB)"}
+
+
+def decode_config(args, world: int) -> dict:
+    return dict(DECODE_CONFIG, new_tokens=args.steps, parallelism=f"replicas x{world}")
 
 
 def tl_prompt(rank: int = 0):
@@ -478,13 +474,13 @@ def run_decode_axion(args, d: Dist) -> dict:
         "dtype": "int8 x int8 -> int32 -> fp32 (A8W8), fp16 KV",
         "data": "synthetic (device-generated Q8_0 weights N(0,0.02), norms 1.0; "
                 "random prompt token ids)",
-        "config": dict(DECODE_CONFIG, parallelism=f"replicas x{d.world}",
-                       device_bytes=dev_bytes),
+        "config": decode_config(args, d.world),
+        "device_bytes": dev_bytes,
         "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": round(TL_PROMPT * 4 / K_new, 3),
                 "d2h_bytes_per_step": 4,
                 "path": "axdec_generate (C ABI): host prompt in, host tokens out, "
-                        "prompt positions included"},
+                        "batched prefill of the prompt included"},
         "roofline": roofline,
         "gpu_launches": step_kernels * K_new,
         "kernels_per_step": step_kernels,
@@ -496,19 +492,18 @@ def run_decode_axion(args, d: Dist) -> dict:
 
 def decode_reference(args, steps: int) -> dict:
     """ModelRunner::generate of the reference on a GGUF with the same weights
-    (the oracle's generator reproduces the device weights bit for bit), on the
-    host cores.  Bounded sample: a short prompt + `steps` new tokens; every
-    position costs one decode_step (the reference prefills token by token),
-    so the rate is positions processed per second."""
-    import ctypes as C
+    (the oracle's generator reproduces the device weights bit for bit; the
+    per-tensor seeds come from the library-free tensor_index), on the host
+    cores.  Bounded sample: a 1-token prompt and `steps` new tokens, i.e.
+    `steps` decode_step calls, each re-reading and dequantizing the 1.1 GB of
+    Q8_0 weights as the reference does for every token (its prompt positions
+    cost the same as generated ones), so the rate is tokens per second of
+    decode_step."""
     import numpy as np
-    from axion_b200 import _lib
-    from axion_b200.decoder import DecoderConfig
+    from axion_b200.decoder import tensor_index
     from axion_b200.gguf import F32, Q8_0, GGUFWriter
     from oracle.oracle import Oracle, RefLib
     o, r = Oracle(), RefLib()
-    lib = _lib.load()
-    cc = DecoderConfig(**TL, max_ctx=TL_PROMPT + TL_NEW).c()
     H, F, V = TL["hidden"], TL["ffn"], TL["vocab"]
     hq = TL["n_heads"] * TL["head_dim"]
     hkv = TL["n_kv_heads"] * TL["head_dim"]
@@ -523,7 +518,7 @@ def decode_reference(args, steps: int) -> dict:
     g.add_f32("llama.attention.layer_norm_rms_epsilon", TL["rms_eps"])
 
     def q8(name, N, K):
-        seed = TL_SEED + lib.axdec_tensor_index(C.byref(cc), name.encode())
+        seed = TL_SEED + tensor_index(TL["n_layers"], name)
         g.add_tensor(name, o.synth_q8_0(seed, N, K, TL_STD), (N, K), Q8_0)
 
     ones = np.ones(H, np.float32)
@@ -544,20 +539,19 @@ def decode_reference(args, steps: int) -> dict:
     tmp = Path(tempfile.mkdtemp()) / "tinyllama_arch_q8_0.gguf"
     g.write(tmp)
     del g
-    prompt = tl_prompt(0)[:2]
+    prompt = tl_prompt(0)[:1]
     sec, toks = r.time_generate(tmp, prompt, steps)
     tmp.unlink()
-    positions = len(prompt) + steps
-    return {"value": round(positions / sec, 4), "unit": "tokens/s", "cores": host_cores(),
+    return {"value": round(steps / sec, 4), "unit": "tokens/s", "cores": host_cores(),
             "kind": "reference",
-            "sample": f"ModelRunner::generate, {len(prompt)}-token prompt + {steps} new tokens "
-                      f"({positions} decode_step calls, each re-reading and dequantizing the "
-                      f"1.1 GB of Q8_0 weights), OpenMP threads={host_cores()}",
-            "seconds": round(sec, 3), "steps": positions}
+            "sample": f"ModelRunner::generate, 1-token prompt + {steps} new tokens ({steps} "
+                      f"decode_step calls, each re-reading and dequantizing the 1.1 GB of Q8_0 "
+                      f"weights), OpenMP threads={host_cores()}; tokens/s = {steps} / seconds",
+            "seconds": round(sec, 3), "steps": steps, "step_seconds": round(sec / steps, 4)}
 
 
 # ---------------------------------------------------------------------------
-# Llama-3-8B-architecture batched decode, tensor parallel
+# Llama-3-8B-architecture batched decode (batch 64, 2048-token prompts), tensor parallel
 # ---------------------------------------------------------------------------
 
 L3 = dict(n_layers=32, hidden=4096, ffn=14336, n_heads=32, n_kv_heads=8, head_dim=128,
@@ -566,17 +560,27 @@ L3_BATCH, L3_PROMPT, L3_NEW, L3_SEED = 64, 2048, 128, 0x8B
 L3_METRIC = "Llama-3-8B-arch Q8_0 batched decode tokens/s (batch 64, 2048-token prompts, greedy)"
 L3_CONFIG = {"workload": "llama3_8b_arch_decode_b64_tp", "layers": 32, "hidden": 4096,
              "ffn": 14336, "heads": "32q/8kv x 128", "vocab": 128256, "rope_theta": 500000.0,
-             "batch": L3_BATCH, "prompt": L3_PROMPT, "new_tokens": L3_NEW,
-             "kv": "paged fp16, block 16", "act": "q8 (A8W8, skinny mma.sync int8 product at M = 64)"}
+             "weights": "Q8_0", "batch": L3_BATCH, "prompt": L3_PROMPT, "new_tokens": L3_NEW,
+             "kv": "paged fp16, block 16",
+             "l2_policy": "7.97 GB of weights + 17.7 GB of KV per step >> L2 (126 MB)"}
+# Q8_0 weights one token streams: 32 layers x (Q, K, V, O, gate, up, down) + LM head
+L3_LAYER_PARAMS = 4096 * 4096 * 2 + 2 * 1024 * 4096 + 3 * 14336 * 4096
+L3_TOKEN_PARAMS = 32 * L3_LAYER_PARAMS + 128256 * 4096
+
+
+def llama3_config(args, world: int) -> dict:
+    return dict(L3_CONFIG, prompt=args.prompt or L3_PROMPT, new_tokens=args.steps,
+                parallelism=f"tp{world}")
 
 
 def run_llama3_axion(args, d: Dist) -> dict:
     """One step = one greedy decode position of all 64 sequences; the job is
     tensor parallel over the N ranks (every rank holds 1/N of each layer's
     heads, FFN rows and LM-head vocabulary), so the whole job decodes 64
-    tokens per step (strong scaling).  The 2048-token prompts are processed
-    by the same step inside the timed call (excluded from `value`, included
-    in `e2e`)."""
+    tokens per step (strong scaling).  The 64 prompts are prefilled in one
+    batched pass (timed apart, reported as `prefill`); then W warm-up and K
+    timed steps through axdec_decode_step with pinned host tokens (`e2e`),
+    then W + K steps continued on the device (`value`)."""
     import numpy as np
     import torch
     from axion_b200 import ops
@@ -585,63 +589,97 @@ def run_llama3_axion(args, d: Dist) -> dict:
     torch.cuda.set_device(dev)
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
-    K_new, P = args.steps, args.prompt or L3_PROMPT
-    cfg = DecoderConfig(**L3, max_batch=L3_BATCH, max_ctx=P + max(K_new, args.warmup),
+    K_new, W, P = args.steps, args.warmup, args.prompt or L3_PROMPT
+    cfg = DecoderConfig(**L3, max_batch=L3_BATCH, max_ctx=P + 2 * (W + K_new) + 1,
                         act_mode="q8", tp_size=d.world, tp_rank=d.rank)
     dec = Decoder(cfg)
     dec.init_random(L3_SEED, 0.02)
     dec.tp_connect()
     prompts = np.random.default_rng(99).integers(0, L3["vocab"], (L3_BATCH, P)).astype(np.int32)
     sp = stream.cuda_stream
-    dec.generate(prompts[:, :8], args.warmup, stream=sp)      # graph build + W steps
+    dec.generate(prompts[:, :8], W, stream=sp)      # step graph + prefill buffers + W steps
     torch.cuda.synchronize()
-    clocks = ClockSampler(device_uuid(dev), period_ms=50).start()
+    d.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    # batched prefill of positions 0 .. P - 2 of every prompt
+    e0.record(stream)
+    dec.prefill(prompts[:, :-1], stream=sp)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    prefill_ms = d.max(e0.elapsed_time(e1))
+    # e2e: the public step call, host tokens in and out (pinned), every step
+    tin = torch.empty(L3_BATCH, dtype=torch.int32, pin_memory=True)
+    tout = torch.empty(L3_BATCH, dtype=torch.int32, pin_memory=True)
+    tin.copy_(torch.from_numpy(prompts[:, -1].copy()))
+    for _ in range(W):
+        dec.decode_step_ptr(tin.data_ptr(), L3_BATCH, tout.data_ptr(), stream=sp)
+        tin.copy_(tout)
+    torch.cuda.synchronize()
+    d.barrier()
+    e0.record(stream)
+    for _ in range(K_new):
+        dec.decode_step_ptr(tin.data_ptr(), L3_BATCH, tout.data_ptr(), stream=sp)
+        tin.copy_(tout)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = d.max(e0.elapsed_time(e1))
+    # value: the same steps continued on the device, inputs resident
+    dec.decode_continue(W, L3_BATCH, first=tin.numpy(), stream=sp)
+    torch.cuda.synchronize()
+    clocks = ClockSampler(device_uuid(dev), period_ms=20).start()
     time.sleep(0.15)
     d.barrier()
     torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    toks, _, decode_ms = dec.generate(prompts, K_new, stream=sp)
-    e1.record(stream)
+    toks, decode_ms = dec.decode_continue(K_new, L3_BATCH, stream=sp)
     torch.cuda.synchronize()
     d.barrier()
     clk = clocks.stop()
     ms_max = d.max(decode_ms)
-    e2e_ms = d.max(e0.elapsed_time(e1))
     n_tok = L3_BATCH * K_new
     value = n_tok / (ms_max / 1e3)
     e2e_val = n_tok / (e2e_ms / 1e3)
-    # roofline per rank: its weight slice + its KV heads read per step
+    # roofline per rank: its weight slice + its KV heads read per step, at the
+    # mean context of the timed steps
     wbytes = dec.weight_bytes_per_step
     kv_l = L3["n_kv_heads"] // d.world
-    mean_ctx = P + (K_new - 1) / 2
+    mean_ctx = P + 2 * W + K_new + (K_new - 1) / 2
     kv_bytes = L3["n_layers"] * 2 * mean_ctx * kv_l * L3["head_dim"] * 2 * L3_BATCH
     step_ms = ms_max / K_new
     achieved = (wbytes + kv_bytes) / (step_ms / 1e3) / 1e9
     peaks, peak_kind = measured_peaks()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": None, "kernel": "decode step per rank (q8_mmq_kernel dominant)",
+                "traffic": ncu_traffic(f"{L3_CONFIG['workload']}_tp{d.world}"),
+                "kernel": "decode step per rank (q8_mmq_kernel dominant)",
                 "step_us": round(step_ms * 1e3, 1),
                 "algorithmic_bytes_per_step_per_rank": int(wbytes + kv_bytes),
+                "weight_bytes_per_step_per_rank": int(wbytes),
+                "kv_bytes_per_step_per_rank": int(kv_bytes),
                 "peak_source": peak_kind}
     status = ops.status()
-    dev_bytes = dec.device_bytes
     kernels = dec.step_kernels(L3_BATCH)
+    dev_bytes = dec.device_bytes
     dec.close()
+    pre_tok = L3_BATCH * (P - 1)
     return {
         "metric": L3_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": d.world,
-        "steps": K_new, "warmup": args.warmup, "ms_per_step": round(step_ms, 4),
+        "steps": K_new, "warmup": W, "ms_per_step": round(step_ms, 4),
         "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int8 x int8 -> int32 -> fp32 (A8W8), fp16 KV",
         "data": "synthetic (device-generated Q8_0 weights N(0,0.02), norms 1.0; "
                 "random prompt token ids)",
-        "config": dict(L3_CONFIG, prompt=P, parallelism=f"tp{d.world} (NCCL all-reduce after "
-                       "O and down, argmax max all-reduce)", device_bytes_per_rank=dev_bytes),
+        "config": llama3_config(args, d.world),
+        "tp": "column-split Q/K/V/gate/up, row-split O/down, vocabulary-split LM head; NCCL "
+              "all-reduce of the hidden state after O and down, max all-reduce of the argmax keys",
+        "device_bytes_per_rank": dev_bytes,
         "e2e": {"value": round(e2e_val, 1), "unit": "tokens/s",
-                "h2d_bytes_per_step": round(L3_BATCH * P * 4 / K_new, 1),
-                "d2h_bytes_per_step": L3_BATCH * 4,
-                "path": "axdec_generate (C ABI), prompt positions included"},
+                "h2d_bytes_per_step": L3_BATCH * 4, "d2h_bytes_per_step": L3_BATCH * 4,
+                "path": "axdec_decode_step (C ABI) per step: pinned host tokens in, H2D, step "
+                        "graph, D2H of the next tokens, synchronize"},
+        "prefill": {"tokens": pre_tok, "ms": round(prefill_ms, 1),
+                    "tokens_per_s": round(pre_tok / (prefill_ms / 1e3), 1),
+                    "path": "axdec_prefill: tcgen05 products over 4096-row chunks + causal "
+                            "attention over the paged cache"},
         "roofline": roofline,
         "gpu_launches": kernels * K_new,
         "kernels_per_step": kernels,
@@ -651,12 +689,15 @@ def run_llama3_axion(args, d: Dist) -> dict:
     }
 
 
-def llama3_reference(args, rows: int) -> dict:
-    """The reference cannot batch decode (rope_apply_row_at takes one row,
-    mha.cpp:208-211), so its rate is extrapolated: load_tensor +
-    linear_from_gguf on one [4096 x 4096] Q8_0 weight at M = `rows`, host
-    cores, gives a multiply-add rate; one batch-64 step needs 64 x (32 layers'
-    218 M + 525 M LM-head weights) multiply-adds."""
+def llama3_reference(args, steps: int) -> dict:
+    """The reference decodes one sequence at a time (no batching:
+    rope_apply_row_at takes one row, mha.cpp:208-211) and, per token,
+    re-reads and dequantizes every weight before its M = 1 product
+    (streaming_executor.cpp:299-307): its per-token cost is that of
+    GGUFLoader::load_tensor + linear_from_gguf at M = 1 over all the weights.
+    Each step times that on one [4096 x 4096] Q8_0 weight (host cores); the
+    rate is extrapolated by weight count to a whole token (32 layers + LM
+    head), attention excluded (which favours the reference)."""
     import numpy as np
     from axion_b200.gguf import Q8_0, GGUFWriter
     from oracle.oracle import Oracle, RefLib
@@ -665,20 +706,21 @@ def llama3_reference(args, rows: int) -> dict:
     gw = GGUFWriter()
     gw.add_tensor("blk.0.attn_q.weight", o.synth_q8_0(L3_SEED, 4096, 4096), (4096, 4096), Q8_0)
     gw.write(tmp)
-    x = np.random.default_rng(0).normal(0, 1, (rows, 4096)).astype(np.float32)
-    r.time_linear(tmp, "blk.0.attn_q.weight", x[:1], 4096, 1)
-    sec, _ = r.time_linear(tmp, "blk.0.attn_q.weight", x, 4096, 1)
+    x = np.random.default_rng(0).normal(0, 1, (1, 4096)).astype(np.float32)
+    for _ in range(max(1, args.warmup)):
+        r.time_linear(tmp, "blk.0.attn_q.weight", x, 4096, 1)
+    secs = [r.time_linear(tmp, "blk.0.attn_q.weight", x, 4096, 1)[0] for _ in range(steps)]
     tmp.unlink()
-    mac_rate = rows * 4096 * 4096 / sec
-    layer = 4096 * 4096 * 2 + 2 * 1024 * 4096 + 3 * 14336 * 4096
-    step_macs = L3_BATCH * (32 * layer + L3["vocab"] * 4096)
-    step_s = step_macs / mac_rate
-    return {"value": round(L3_BATCH / step_s, 5), "unit": "tokens/s", "cores": host_cores(),
-            "kind": "reference",
-            "sample": f"extrapolated: load_tensor + linear_from_gguf [4096x4096] Q8_0 at M={rows} "
-                      f"({sec:.2f} s, OpenMP threads={host_cores()}) scaled to one batch-64 "
-                      f"Llama-3-8B step ({step_macs / 1e12:.2f} T multiply-adds)",
-            "seconds": round(step_s, 3), "steps": 1}
+    per_weight = statistics.mean(secs) / (4096 * 4096)
+    token_s = per_weight * L3_TOKEN_PARAMS
+    return {"value": round(1.0 / token_s, 5), "unit": "tokens/s", "cores": host_cores(),
+            "kind": "reference", "extrapolated": True,
+            "sample": f"each step: GGUFLoader::load_tensor + linear_from_gguf, [4096x4096] Q8_0, "
+                      f"M=1 (OpenMP threads={host_cores()}, mean {statistics.mean(secs):.3f} s); "
+                      f"tokens/s = 1 / (that time x {L3_TOKEN_PARAMS / 4096**2:.1f}, the weights "
+                      f"one token streams / 4096^2), sequences one at a time",
+            "seconds": round(sum(secs), 3), "steps": steps,
+            "step_seconds": round(statistics.mean(secs), 4)}
 
 
 # ---------------------------------------------------------------------------
@@ -821,10 +863,7 @@ def run_skinny_axion(args, d: Dist) -> dict:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 x int8 -> int32 -> fp32 (mma.sync m16n8k32)",
         "data": "synthetic (device-generated Q8_0 weights N(0,0.02); x N(0,1))",
-        "config": dict(SKINNY_CONFIG, act="q8 (pre-quantized, transposed scales)",
-                       l2_policy="221 MB of weights per pass, each weight reused only after "
-                                 "the other three (> L2)",
-                       parallelism=f"replicas x{d.world}"),
+        "config": skinny_config(args, d.world),
         "e2e": {"value": round(e2e_val, 1), "unit": "GB/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "steps": n_e2e,
                 "path": "axq8_linear (C ABI, A8, width dispatch) + pinned H2D/D2H per product"},
@@ -859,7 +898,7 @@ def skinny_reference(args, rows: int) -> dict:
 
 
 # ---------------------------------------------------------------------------
-# Prefill GEMM sweep (BASELINE config 3): Llama-2-7B linear shapes on the
+# Prefill GEMM sweep: Llama-2-7B linear shapes on the
 # tensor-core path
 # ---------------------------------------------------------------------------
 
@@ -991,8 +1030,7 @@ def run_prefill_axion(args, d: Dist) -> dict:
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int8 x int8 -> int32 (tcgen05 kind::i8) -> fp32 per-block rescale",
         "data": "synthetic (device-generated Q8_0 weights N(0,0.02); activations N(0,1))",
-        "config": dict(PREFILL_CONFIG, parallelism=f"replicas x{d.world}",
-                       l2_policy="cases in rotation, 253 MB of weights > L2"),
+        "config": prefill_config(args, d.world),
         "e2e": {"value": round(e2e_val, 1), "unit": "TOPS", "h2d_bytes_per_step": h2d // K_steps,
                 "d2h_bytes_per_step": d2h // K_steps,
                 "path": "axq8_linear (C ABI), pinned H2D of x and D2H of y per GEMM"},
@@ -1027,15 +1065,36 @@ def prefill_reference(args, steps: int) -> dict:
             "seconds": round(sec, 3), "steps": 1}
 
 
+def gemv_config(args, world: int) -> dict:
+    return {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K, "M": 1,
+            "weights": "Q8_0", "parallelism": f"replicas x{world}"}
+
+
+def prefill_config(args, world: int) -> dict:
+    return dict(PREFILL_CONFIG, parallelism=f"replicas x{world}",
+                l2_policy="cases in rotation, 253 MB of weights > L2")
+
+
+def skinny_config(args, world: int) -> dict:
+    return dict(SKINNY_CONFIG, parallelism=f"replicas x{world}",
+                l2_policy="221 MB of weights per pass, each weight reused only after the other "
+                          "three (> L2)")
+
+
 WORKLOADS = {
-    # name: (axion arm, reference/cpu-baseline arm, metric, config, default K, reference sample)
-    "decode": (run_decode_axion, decode_reference, DECODE_METRIC, DECODE_CONFIG, TL_NEW, 3),
+    # name: (axion arm, reference arm, metric, config(args, n_gpus), default K,
+    #        reference sample of the cpu_baseline leg, steps of the reference arm
+    #        (None: K), scaling)
+    "llama3": (run_llama3_axion, llama3_reference, L3_METRIC, llama3_config, L3_NEW, 8, None,
+               "strong"),
+    "decode": (run_decode_axion, decode_reference, DECODE_METRIC, decode_config, TL_NEW, 3, 24,
+               "weak"),
     "gemv": (run_gemv_axion, gemv_reference, "Q8_0 GEMV HBM GB/s (algorithmic bytes)",
-             {"workload": "q8_0_gemv_5632x2048_m1", "N": GEMV_N, "K": GEMV_K, "M": 1},
-             200000, 300),
-    "prefill": (run_prefill_axion, prefill_reference, PREFILL_METRIC, PREFILL_CONFIG, 16, 64),
-    "llama3": (run_llama3_axion, llama3_reference, L3_METRIC, L3_CONFIG, L3_NEW, 16),
-    "skinny": (run_skinny_axion, skinny_reference, SKINNY_METRIC, SKINNY_CONFIG, 20, 16),
+             gemv_config, 200000, 300, 300, "weak"),
+    "prefill": (run_prefill_axion, prefill_reference, PREFILL_METRIC, prefill_config, 16, 64, 64,
+                "weak"),
+    "skinny": (run_skinny_axion, skinny_reference, SKINNY_METRIC, skinny_config, 20, 16, 16,
+               "weak"),
 }
 
 
@@ -1045,7 +1104,7 @@ def main() -> int:
     ap.add_argument("--steps", type=int, default=None)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["axion", "reference"], default="axion")
-    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="decode")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3")
     ap.add_argument("--prompt", type=int, default=None,
                     help="llama3 workload: prompt length (default 2048)")
     ap.add_argument("--cpu-sample", type=int, default=None,
@@ -1053,31 +1112,36 @@ def main() -> int:
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
-    run_axion, run_ref, metric, config, k_default, sample_default = WORKLOADS[args.workload]
+    (run_axion, run_ref, metric, config_fn, k_default, sample_default, ref_steps,
+     scaling) = WORKLOADS[args.workload]
+    if args.steps is None:
+        args.steps = k_default
     d = Dist(args.gpus)
 
     if args.impl == "reference":
+        # rank 0 alone, on the host cores; loads no library of this repository
         if d.rank != 0:
             return 0
         use_all_host_cores()
-        sample = args.cpu_sample or sample_default
+        sample = args.cpu_sample or (ref_steps if ref_steps is not None else args.steps)
         cb = run_ref(args, sample)
         steps = cb.get("steps", sample)
+        step_s = cb.get("step_seconds", cb["seconds"] / steps)
         out = {"impl": "reference", "metric": metric, "value": cb["value"], "unit": cb["unit"],
                "n_gpus": args.gpus, "steps": steps, "warmup": args.warmup,
-               "ms_per_step": round(cb["seconds"] * 1e3 / steps, 3),
-               "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+               "ms_per_step": round(step_s * 1e3, 3),
+               "higher_is_better": True, "scaling": scaling, "vs_baseline": None,
                "dtype": "fp32 (the reference dequantizes Q8_0 to fp32)",
                "data": "synthetic (host-generated Q8_0 GGUF, same weights as the axion arm)",
-               "config": dict(config, parallelism=f"host OpenMP x{cb['cores']}"),
+               "config": config_fn(args, args.gpus),
+               "reference_run": f"host OpenMP x{cb['cores']}, rank 0 only: {cb['sample']}",
+               "extrapolated": bool(cb.get("extrapolated", False)),
                "cpu_baseline": {k: cb[k] for k in ("value", "unit", "cores", "kind", "sample")},
                "e2e": {"value": cb["value"], "unit": cb["unit"], "h2d_bytes_per_step": 0,
                        "d2h_bytes_per_step": 0}}
         print(json.dumps(out))
         return 0
 
-    if args.steps is None:
-        args.steps = k_default
     d.init("nccl")
     res = run_axion(args, d)
     if d.rank == 0:
