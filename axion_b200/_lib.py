@@ -102,6 +102,10 @@ SIGNATURES: dict[str, tuple] = {
                                       _P]),
     "axkv_paged_prefill_attn": (_I32, [C.POINTER(axkv_cache_t), _P, _I64, _I32, _I32, _I32, _I32,
                                        _P, _P, _P, _P]),
+    "axtp_allreduce_sum": (_I32, [_P, _I64, _P]),
+    "axdec_tp_allreduce_kind": (_I32, [_P]),
+    "axdec_tp_health": (_I32, [_P, C.POINTER(C.c_int), C.POINTER(C.c_int)]),
+    "axdec_tp_abort": (_I32, [_P]),
     "axdec_set_prefill": (_I32, [_P, _I32]),
     "axdec_prefill_batched": (_I32, [_P, _I32]),
     "axdec_prefill": (_I32, [_P, _P, _I32, _I32, _P]),

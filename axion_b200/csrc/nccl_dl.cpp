@@ -38,8 +38,11 @@ const NcclApi* nccl_api() {
         api.CommDestroy = (decltype(api.CommDestroy))dlsym(h, "ncclCommDestroy");
         api.AllReduce = (decltype(api.AllReduce))dlsym(h, "ncclAllReduce");
         api.GetErrorString = (decltype(api.GetErrorString))dlsym(h, "ncclGetErrorString");
+        api.AllGather = (decltype(api.AllGather))dlsym(h, "ncclAllGather");
+        api.CommGetAsyncError = (decltype(api.CommGetAsyncError))dlsym(h, "ncclCommGetAsyncError");
+        api.CommAbort = (decltype(api.CommAbort))dlsym(h, "ncclCommAbort");
         ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.AllReduce &&
-             api.GetErrorString;
+             api.GetErrorString && api.AllGather && api.CommGetAsyncError && api.CommAbort;
         if (!ok) snprintf(why, sizeof(why), "NCCL library lacks an entry point");
     });
     if (!ok) {

@@ -15,6 +15,11 @@ struct NcclApi {
     ncclResult_t (*AllReduce)(const void*, void*, size_t, ncclDataType_t, ncclRedOp_t, ncclComm_t,
                               cudaStream_t);
     const char* (*GetErrorString)(ncclResult_t);
+    ncclResult_t (*AllGather)(const void*, void*, size_t, ncclDataType_t, ncclComm_t, cudaStream_t);
+    // failure handling: the communicator's asynchronous error, and abort
+    // (ends pending NCCL work so that a rank whose peer died can exit)
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t*);
+    ncclResult_t (*CommAbort)(ncclComm_t);
 };
 
 // The loaded API, or nullptr (with the error recorded for axq8_last_error).

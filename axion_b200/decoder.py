@@ -128,6 +128,21 @@ class Decoder:
         buf = (C.c_ubyte * len(uid)).from_buffer_copy(uid)
         check(self.lib.axdec_tp_connect(self.h, C.cast(buf, C.c_void_p)))
 
+    @property
+    def tp_allreduce(self) -> str:
+        """Hidden-state all-reduce in use: "none", "nccl" or "nvlink"."""
+        return ("none", "nccl", "nvlink")[self.lib.axdec_tp_allreduce_kind(self.h)]
+
+    def tp_health(self) -> tuple[int, int]:
+        """(NCCL asynchronous error, device status word), without a device sync."""
+        e, st = C.c_int(0), C.c_int(0)
+        check(self.lib.axdec_tp_health(self.h, C.byref(e), C.byref(st)))
+        return e.value, st.value
+
+    def tp_abort(self) -> None:
+        """Abort the communicator (a peer failed); tp_connect again before stepping."""
+        check(self.lib.axdec_tp_abort(self.h))
+
     def _new_id(self) -> bytes:
         buf = (C.c_ubyte * 128)()
         check(self.lib.axdec_tp_unique_id(C.cast(buf, C.c_void_p), 128))

@@ -155,6 +155,24 @@ int64_t axdec_weight_bytes_per_step(const axdec_model_t* m);
 int axdec_tp_unique_id(void* id_out, int64_t id_bytes);
 int axdec_tp_connect(axdec_model_t* m, const void* id);
 
+/* The hidden-state all-reduce of a connected model: 0 none (tp_size 1), 1 NCCL
+ * (default), 2 the NVLink peer-memory kernel of axtp.h, which
+ * axdec_tp_connect sets up when AXDEC_TP_AR=nvlink and every rank can map the
+ * others' buffers with CUDA IPC: each rank sums its slice of the partials in
+ * rank order and writes it to every rank, so all ranks hold identical sums;
+ * its waits on the peers are bounded (about two seconds), after which the
+ * device status word reads AXQ8_ERR_WAIT_TIMEOUT. */
+int axdec_tp_allreduce_kind(const axdec_model_t* m);
+
+/* Failure handling.  axdec_tp_health reads, without synchronizing the device,
+ * the communicator's asynchronous error (ncclResult_t, 0 = none) and the
+ * device status word (AXQ8_ERR_WAIT_TIMEOUT after a peer stopped answering).
+ * axdec_tp_abort aborts the communicator (ncclCommAbort), which ends pending
+ * NCCL work so that a rank whose peer failed can return; the model then needs
+ * a new axdec_tp_connect before the next step. */
+int axdec_tp_health(axdec_model_t* m, int* nccl_error, int* device_status);
+int axdec_tp_abort(axdec_model_t* m);
+
 /* Kernels launched by one decode step of n_seq sequences: the kernel nodes
  * of the step's CUDA graph, captured by the first axdec_generate/axdec_forced
  * call with that n_seq (-1 before it). */

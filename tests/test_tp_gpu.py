@@ -62,7 +62,9 @@ def _run(fn, world, *args):
     mp.spawn(fn, args=(world, _port()) + args, nprocs=world, join=True)
 
 
-def _gather(out, world):
+def _gather(out, world, ar=None):
+    if ar is not None:       # the all-reduce every rank connected with
+        assert [(out / f"ar{r}.txt").read_text() for r in range(world)] == [ar] * world
     toks = [np.load(out / f"tok{r}.npy") for r in range(world)]
     lgs = [np.load(out / f"lg{r}.npy") for r in range(world)]
     for t in toks[1:]:
@@ -70,8 +72,9 @@ def _gather(out, world):
     return toks[0], np.concatenate(lgs, axis=-1)   # vocabulary slices in rank order
 
 
+@pytest.mark.parametrize("ar", ["nvlink", "nccl"])
 @pytest.mark.parametrize("world", [2, 4])
-def test_tp_f32_matches_single_gpu(cuda, tmp_path, world):
+def test_tp_f32_matches_single_gpu(cuda, tmp_path, world, ar):
     _need(world)
     import _tp_worker
     from axion_b200.decoder import Decoder
@@ -82,8 +85,8 @@ def test_tp_f32_matches_single_gpu(cuda, tmp_path, world):
     rt, rl, _ = ref.generate(prompt, 12, logits=True)
     ref.close()
     _run(_tp_worker.tiny_gguf, world, str(tmp_path), str(golden("tiny_llama.gguf")), "f32", True,
-         prompt, 12)
-    toks, lg = _gather(tmp_path, world)
+         prompt, 12, ar)
+    toks, lg = _gather(tmp_path, world, ar)
     assert np.array_equal(toks, rt)
     assert _rel(lg[:, 0, :], rl[:, 0, :]) <= TP_F32_TOL
 
@@ -130,3 +133,30 @@ def test_tp_tinyllama_architecture_batch(cuda, tmp_path, world):
     assert err <= A8_TOL
     for b in range(3):
         assert _top1_consistent(lg[:, b, :], rl[:, b, :], A8_TOL)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_llama3_head_shape_wide_batch_with_prefill(cuda, tmp_path, world):
+    """Head dim 128 with 4 query heads per KV head (the Llama-3 head shape), 16
+    sequences (the wide step: skinny products, the NVLink all-reduce) and
+    40-token prompts through the batched prefill (tcgen05 products, NCCL
+    all-reduce of the chunk): every rank agrees with one GPU teacher-forced
+    with the run's tokens."""
+    _need(world)
+    import _tp_worker
+    from axion_b200.decoder import Decoder, DecoderConfig
+    kw = dict(n_layers=2, hidden=1024, ffn=2048, n_heads=16, n_kv_heads=4, head_dim=128,
+              vocab=4096, rope_theta=500000.0, rms_eps=1e-5, max_batch=16, max_ctx=64)
+    prompts = np.random.default_rng(7).integers(0, 4096, (16, 40)).astype(np.int32)
+    _run(_tp_worker.synthetic, world, str(tmp_path), kw, 0x8B, prompts.tolist(), 4, "nvlink")
+    toks, lg = _gather(tmp_path, world, "nvlink")
+    ref = Decoder(DecoderConfig(**kw))
+    ref.init_random(0x8B, std=0.02)
+    rl = ref.forced(np.concatenate([prompts, toks[:, :-1]], axis=1), prompts.shape[1])
+    ref.close()
+    err = _rel(lg.reshape(4, -1), rl.reshape(4, -1))
+    print(f"tp{world} llama3-head-shape b16 logits rel err vs 1 GPU: {err:.2e}")
+    assert err <= A8_TOL
+    for b in range(16):
+        assert _top1_consistent(lg[:, b, :], rl[:, b, :], A8_TOL)
+

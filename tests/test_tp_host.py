@@ -47,3 +47,32 @@ def test_id_exchange_two_gloo_ranks(tmp_path):
     mp.spawn(_tp_worker.id_exchange, args=(2, _port(), str(tmp_path)), nprocs=2, join=True)
     ids = [(tmp_path / f"id{r}.bin").read_bytes() for r in range(2)]
     assert ids[0] == ids[1] == bytes(range(128))
+
+
+def test_peer_that_leaves_is_detected_before_the_next_step(tmp_path):
+    """Two gloo ranks exchange heartbeats between steps; rank 1 leaves
+    without a word, rank 0 sees its heartbeat go stale before its next step,
+    aborts the (fake) communicator and stops."""
+    import torch.multiprocessing as mp
+    import _tp_worker
+    mp.spawn(_tp_worker.heartbeat_failure, args=(2, _port(), str(tmp_path), 5, 0.5), nprocs=2,
+             join=True)
+    outcome = (tmp_path / "outcome0.txt").read_text()
+    assert outcome.startswith("peer failure [1]") and outcome.endswith("aborted True"), outcome
+    assert (tmp_path / "left1.txt").exists()
+
+
+def test_heartbeat_marks_a_silent_peer():
+    from axion_b200.tp_watchdog import Heartbeat
+    import time
+    import torch.distributed as dist
+    store = dist.HashStore()
+    a = Heartbeat(store, 0, 2, timeout=0.2)
+    b = Heartbeat(store, 1, 2, timeout=0.2)
+    a.beat()
+    b.beat()
+    assert a.dead_peers() == [] and b.dead_peers() == []
+    time.sleep(0.3)
+    a.beat()
+    assert a.dead_peers() == [1]        # rank 1 stopped beating
+    assert b.dead_peers() == []         # rank 0 is fresh
