@@ -96,6 +96,21 @@ def ncu_traffic(workload: str):
         return None
 
 
+def l3_traffic(layers: int, world: int, kv_bytes: float):
+    """DRAM bytes of one Llama-3-8B decode step on one GPU: the measured
+    per-layer and embedding/LM-head traffic of profiles/ncu_traffic.json
+    (a 4-layer capture) scaled to `layers`, plus the K/V pages the step reads;
+    None for tensor-parallel ranks (not captured: ncu runs one process)."""
+    p = ROOT / "profiles" / "ncu_traffic.json"
+    try:
+        t = json.loads(p.read_text())["llama3_8b_arch_decode_b64_tp1"]
+    except Exception:
+        return None
+    if world != 1:
+        return None
+    return int(layers * t["per_layer_bytes"] + t["embed_head_argmax_bytes"] + kv_bytes)
+
+
 def use_all_host_cores() -> None:
     """The reference's OpenMP loops use every host core (torchrun sets
     OMP_NUM_THREADS=1 for its workers); called before its library loads."""
@@ -569,7 +584,8 @@ L3_TOKEN_PARAMS = 32 * L3_LAYER_PARAMS + 128256 * 4096
 
 
 def llama3_config(args, world: int) -> dict:
-    return dict(L3_CONFIG, prompt=args.prompt or L3_PROMPT, new_tokens=args.steps,
+    return dict(L3_CONFIG, layers=args.layers or L3["n_layers"], prompt=args.prompt or L3_PROMPT,
+                new_tokens=args.steps,
                 parallelism=f"tp{world}")
 
 
@@ -590,7 +606,8 @@ def run_llama3_axion(args, d: Dist) -> dict:
     stream = torch.cuda.Stream(dev)
     torch.cuda.set_stream(stream)
     K_new, W, P = args.steps, args.warmup, args.prompt or L3_PROMPT
-    cfg = DecoderConfig(**L3, max_batch=L3_BATCH, max_ctx=P + 2 * (W + K_new) + 1,
+    arch = dict(L3, n_layers=args.layers or L3["n_layers"])
+    cfg = DecoderConfig(**arch, max_batch=L3_BATCH, max_ctx=P + 2 * (W + K_new) + 1,
                         act_mode="q8", tp_size=d.world, tp_rank=d.rank)
     dec = Decoder(cfg)
     dec.init_random(L3_SEED, 0.02)
@@ -643,13 +660,13 @@ def run_llama3_axion(args, d: Dist) -> dict:
     wbytes = dec.weight_bytes_per_step
     kv_l = L3["n_kv_heads"] // d.world
     mean_ctx = P + 2 * W + K_new + (K_new - 1) / 2
-    kv_bytes = L3["n_layers"] * 2 * mean_ctx * kv_l * L3["head_dim"] * 2 * L3_BATCH
+    kv_bytes = arch["n_layers"] * 2 * mean_ctx * kv_l * L3["head_dim"] * 2 * L3_BATCH
     step_ms = ms_max / K_new
     achieved = (wbytes + kv_bytes) / (step_ms / 1e3) / 1e9
     peaks, peak_kind = measured_peaks()
     roofline = {"bound": "hbm", "achieved": round(achieved, 1), "peak": peaks["hbm_gbs"],
                 "unit": "GB/s", "frac": round(achieved / peaks["hbm_gbs"], 4),
-                "traffic": ncu_traffic(f"{L3_CONFIG['workload']}_tp{d.world}"),
+                "traffic": l3_traffic(arch["n_layers"], d.world, kv_bytes),
                 "kernel": "decode step per rank (q8_mmq_kernel dominant)",
                 "step_us": round(step_ms * 1e3, 1),
                 "algorithmic_bytes_per_step_per_rank": int(wbytes + kv_bytes),
@@ -1105,6 +1122,9 @@ def main() -> int:
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["axion", "reference"], default="axion")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="llama3")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="llama3 workload: decoder layers (default 32; fewer only for small "
+                         "profiler captures, and the config says so)")
     ap.add_argument("--prompt", type=int, default=None,
                     help="llama3 workload: prompt length (default 2048)")
     ap.add_argument("--cpu-sample", type=int, default=None,
