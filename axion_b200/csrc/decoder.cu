@@ -1080,17 +1080,21 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->rs_f = q8r_row_stride(c.ffn);
     m->max_blocks = (c.max_ctx + c.kv_block - 1) / c.kv_block;
     // split the context so that attention gives about four CTAs per SM at full
-    // length, down to one page per split (AXDEC_ATTN_MIN_PAGES overrides,
-    // tuning; measured at batch 1, 384-token context: 1 page 1,202 tokens/s,
-    // 2 pages 1,166, 4 pages 998, one split 710), at most 32 splits (the
-    // merge gives one lane to each split)
-    const int min_pages = [] {
+    // length, at most 32 splits (the merge gives one lane to each split), each
+    // split at least min_pages pages: one page when the (sequence, kv head)
+    // pairs are few (batch 1, 384-token context: 1 page 1,202 tokens/s, 2 pages
+    // 1,166, 4 pages 998, one split 710), 32 pages from 64 pairs on, where the
+    // grid is wide already and more splits only add merge work (batch 64, one
+    // kv head, 2048-token context: 1 page 3.155 ms per step, 32 pages 3.081).
+    // AXDEC_ATTN_MIN_PAGES overrides (tuning).
+    const int pairs = c.n_kv_heads * c.max_batch;
+    const int min_pages = [pairs] {
+        const int dflt = pairs >= 64 ? 32 : 1;
         const char* e = getenv("AXDEC_ATTN_MIN_PAGES");
-        const int v = e ? atoi(e) : 1;
-        return v >= 1 && v <= 4096 ? v : 1;
+        const int v = e ? atoi(e) : dflt;
+        return v >= 1 && v <= 4096 ? v : dflt;
     }();
-    const int target = (4 * ds->sm_count + c.n_kv_heads * c.max_batch - 1) /
-                       (c.n_kv_heads * c.max_batch);
+    const int target = (4 * ds->sm_count + pairs - 1) / pairs;
     m->nsplit = std::max(1, std::min(std::min(target, (m->max_blocks + min_pages - 1) / min_pages), 32));
     m->bps = (m->max_blocks + m->nsplit - 1) / m->nsplit;
     m->nsplit = (m->max_blocks + m->bps - 1) / m->bps;

@@ -105,6 +105,15 @@ int launch_bn(DeviceState* ds, const CUtensorMap& tw, const CUtensorMap& tx, con
         AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                            MmaCfg<BN>::SMEM),
                       "cudaFuncSetAttribute(q8_mma)");
+        if (MmaCfg<BN>::REG_SPLIT) {
+            // the register split must fit the CTA's pool, else setmaxnreg.inc would never return
+            cudaFuncAttributes fa;
+            AXQ8_CUDA_TRY(cudaFuncGetAttributes(&fa, kern), "cudaFuncGetAttributes(q8_mma)");
+            if (fa.numRegs < MmaCfg<BN>::LAUNCH_REGS_MIN)
+                return fail(AXQ8_ERR_UNSUPPORTED,
+                            "tensor-core linear: kernel built with %d registers, register split needs %d",
+                            fa.numRegs, MmaCfg<BN>::LAUNCH_REGS_MIN);
+        }
         configured[dev] = 1;
     }
     AXQ8_CUDA_TRY(launch_k(kern, grid, dim3(MmaCfg<BN>::THREADS), MmaCfg<BN>::SMEM, s, true, tw,

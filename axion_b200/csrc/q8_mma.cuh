@@ -12,19 +12,22 @@
 // kind::i8 MMA consumes exactly K = 32, so every MMA is one block: its
 // int32 result D_b (exact, |D_b| <= 32*128*128 < 2^22) is read back by the
 // epilogue warps, scaled and added to fp32 accumulators held in registers:
-//     t   = D_b * dw   (exact product, one rounding: fma(1.5*2^23 + D_b, dw, -1.5*2^23*dw);
-//                       the D buffer is preset to the bits of 1.5*2^23 and the MMA
-//                       accumulates onto it, so its float view is 1.5*2^23 + D_b)
+//     t   = D_b * dw   (exact product, one rounding: the integer add of the
+//                       bits of 1.5*2^23 turns D_b into the float 1.5*2^23 + D_b,
+//                       then fma(1.5*2^23 + D_b, dw, -1.5*2^23*dw))
 //     acc = fma(t, dx, acc)
-// TMEM holds four D buffers, one per block of a 4-block stage, so the MMAs
-// of the next blocks run while block b is rescaled; the epilogue re-arms a
-// buffer (tcgen05.st of the preset) right after reading it.
+// TMEM holds four D buffers, one per block of a 4-block stage; each MMA
+// overwrites its buffer, and the epilogue hands a buffer back to the MMA
+// issuer as soon as its 32 columns are in registers, so the MMAs of the next
+// blocks run while block b is rescaled.
 //
 // Warp roles: warp 0 lane 0 issues TMA loads (weight quants [128 x 128 B],
 // activation quants [BN x 128 B], transposed activation scales [4 x BN] fp32
-// per 4-block stage), warp 1 lane 0 issues the MMAs, warps 2.. are the
-// epilogue, BN/8 of them (warp w reads TMEM lanes 32*(w%4).. and the 32
-// columns of group (w-2)/4).  Every wait is bounded (WAIT_BUDGET_CYCLES); a
+// per 4-block stage), warp 1 lane 0 issues the MMAs, warps 2-3 idle; warps
+// 4.. are the epilogue, BN/8 of them (warp w reads TMEM lanes 32*(w%4).. and
+// the 32 columns of group (w-4)/4).  For BN >= 64 warpgroup 0 hands registers
+// to the epilogue warpgroups (setmaxnreg), which hold 32 accumulators and 32
+// TMEM values per thread.  Every wait is bounded (WAIT_BUDGET_CYCLES); a
 // wait that gives up records AXQ8_ERR_WAIT_TIMEOUT and its role stops, the
 // CTA then waits (bounded) for its MMAs to retire and frees TMEM.
 //
@@ -66,7 +69,18 @@ struct MmaCfg {
     static constexpr int TMEM_COLS = NBUF * BN;
     static constexpr int CW = 32;                             // columns per epilogue thread
     static constexpr int EPI_WARPS = 4 * (BN / CW);           // 4 lane quarters x column groups
-    static constexpr int THREADS = (2 + EPI_WARPS) * 32;
+    static constexpr int EPI_WARP0 = 4;                       // warpgroup 0: TMA, MMA, two idle warps
+    static constexpr int THREADS = (EPI_WARP0 + EPI_WARPS) * 32;
+    // Register split (setmaxnreg) where the launch cap would make the
+    // epilogue spill: warpgroup 0 gives registers back, the epilogue
+    // warpgroups take them.  The CTA's pool is THREADS x the launch register
+    // count, which the launcher checks against LAUNCH_REGS_MIN before launching
+    // (setmaxnreg.inc waits until the pool can serve it).
+    static constexpr bool REG_SPLIT = BN >= 64;
+    static constexpr int REGS_WG0 = 32;
+    static constexpr int REGS_EPI = BN == 128 ? 112 : 104;
+    static constexpr int LAUNCH_REGS_MIN =
+        (128 * REGS_WG0 + EPI_WARPS * 32 * REGS_EPI + THREADS - 1) / THREADS;
 };
 
 struct MmaArgs {
@@ -117,35 +131,40 @@ __device__ inline void mma_i8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
         "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
-// 16 consecutive 32-bit TMEM columns of this warp's 32 lanes.
-__device__ inline void tmem_ld16(uint32_t taddr, uint32_t* r) {
+// 32 consecutive 32-bit TMEM columns of this warp's 32 lanes, and the wait
+// for them: the registers of the load are tied to the wait so no use of
+// them is scheduled before it.
+__device__ inline void tmem_ld32(uint32_t taddr, uint32_t* r) {
     asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, "
-        "%11, %12, %13, %14, %15}, [%16];"
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
         : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
           "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
-          "=r"(r[14]), "=r"(r[15])
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]),
+          "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]),
+          "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
         : "r"(taddr));
 }
-// Wait for this thread's TMEM loads; the 16 registers of the load being
-// waited for are tied to the wait so no use of them is scheduled before it.
-__device__ inline void tmem_wait_ld16(uint32_t* r) {
+__device__ inline void tmem_wait_ld32(uint32_t* r) {
     asm volatile("tcgen05.wait::ld.sync.aligned;"
                  : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]),
                    "+r"(r[6]), "+r"(r[7]), "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]),
-                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                   "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15]), "+r"(r[16]), "+r"(r[17]),
+                   "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]), "+r"(r[23]),
+                   "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                   "+r"(r[30]), "+r"(r[31])
                  :
                  : "memory");
 }
-// Store one value into 16 consecutive TMEM columns of this warp's 32 lanes.
-__device__ inline void tmem_st16_const(uint32_t taddr, uint32_t v) {
-    asm volatile(
-        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %1, %1, %1, %1, %1, %1, %1, %1, %1, "
-        "%1, %1, %1, %1, %1, %1};" ::"r"(taddr),
-        "r"(v)
-        : "memory");
+template <int N>
+__device__ inline void setmaxnreg_dec() {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
-__device__ inline void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+template <int N>
+__device__ inline void setmaxnreg_inc() {
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
 
 // 2-D tiled TMA load (no multicast) into shared memory, completion as
 // transaction bytes on `bar`.  x (innermost) must be a multiple of 16 bytes.
@@ -229,17 +248,6 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tmem_slot;
-    // Every D buffer starts at 1.5*2^23 as fp32 bits; the MMAs accumulate the
-    // block dot onto it, so the float view of a result is 1.5*2^23 + D_b.
-    if (warp >= 2) {
-        const uint32_t tq = tmem + ((uint32_t)((warp & 3) * 32) << 16) + ((warp - 2) >> 2) * CW;
-#pragma unroll
-        for (int b = 0; b < NB; b++) {
-#pragma unroll
-            for (int c = 0; c < CW; c += 16) tmem_st16_const(tq + b * BN + c, kMagicBits);
-        }
-        tmem_wait_st();
-    }
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -252,51 +260,55 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
         return reinterpret_cast<float*>(smem + s * C::STAGE + C::W_BYTES + C::X_BYTES);
     };
 
-    if (warp == 0) {
-        if (lane == 0) {
-            int issued = 0;
-            for (int i = 0; i < nst; i++) {
-                const int s = i % S, u = i / S;
-                if (!wait_or_flag(&empty[s], (u & 1) ^ 1, a.status, abort)) break;
-                mbar_arrive_expect_tx(&full[s], C::W_BYTES + C::X_BYTES + C::D_BYTES);
-                const int st = st0 + i;
-                tma_load_2d(stage_w(s), &tm_w, st * kMmaKC, n0, &full[s]);
-                tma_load_2d(stage_x(s), &tm_x, st * kMmaKC, m0, &full[s]);
-                tma_load_2d(stage_d(s), &tm_d, m0, st * 4, &full[s]);
-                issued++;
-            }
-            // no copy may still be landing when the CTA exits
-            for (int i = max(0, issued - S); i < issued; i++)
-                mbar_wait_bounded(&full[i % S], (i / S) & 1, a.status, AXQ8_ERR_WAIT_TIMEOUT);
-        }
-    } else if (warp == 1) {
-        if (lane == 0) {
-            const uint32_t idesc = mma_i8_idesc(kMmaBM, BN);
-            for (int i = 0; i < nst; i++) {
-                const int s = i % S, u = i / S;
-                if (!wait_or_flag(&full[s], u & 1, a.status, abort)) break;
-                tc_fence_after();
-                const uint64_t ad = sw128_kmajor_desc(smem_u32(stage_w(s)));
-                const uint64_t bd = sw128_kmajor_desc(smem_u32(stage_x(s)));
-                bool ok = true;
-                for (int k4 = 0; k4 < 4; k4++) {       // D buffer k4 holds block 4i+k4
-                    if (!wait_or_flag(&tempty[k4], (i & 1) ^ 1, a.status, abort)) {
-                        ok = false;
-                        break;
-                    }
-                    tc_fence_after();
-                    mma_i8(tmem + k4 * BN, ad + 2 * k4, bd + 2 * k4, idesc, 1);
-                    tc_commit(&tfull[k4]);
+    if (warp < C::EPI_WARP0) {
+        if (C::REG_SPLIT) setmaxnreg_dec<C::REGS_WG0>();
+        if (warp == 0) {
+            if (lane == 0) {
+                int issued = 0;
+                for (int i = 0; i < nst; i++) {
+                    const int s = i % S, u = i / S;
+                    if (!wait_or_flag(&empty[s], (u & 1) ^ 1, a.status, abort)) break;
+                    mbar_arrive_expect_tx(&full[s], C::W_BYTES + C::X_BYTES + C::D_BYTES);
+                    const int st = st0 + i;
+                    tma_load_2d(stage_w(s), &tm_w, st * kMmaKC, n0, &full[s]);
+                    tma_load_2d(stage_x(s), &tm_x, st * kMmaKC, m0, &full[s]);
+                    tma_load_2d(stage_d(s), &tm_d, m0, st * 4, &full[s]);
+                    issued++;
                 }
-                if (!ok) break;
-                tc_commit(&empty[s]);
+                // no copy may still be landing when the CTA exits
+                for (int i = max(0, issued - S); i < issued; i++)
+                    mbar_wait_bounded(&full[i % S], (i / S) & 1, a.status, AXQ8_ERR_WAIT_TIMEOUT);
             }
-            tc_commit(done);
+        } else if (warp == 1) {
+            if (lane == 0) {
+                const uint32_t idesc = mma_i8_idesc(kMmaBM, BN);
+                for (int i = 0; i < nst; i++) {
+                    const int s = i % S, u = i / S;
+                    if (!wait_or_flag(&full[s], u & 1, a.status, abort)) break;
+                    tc_fence_after();
+                    const uint64_t ad = sw128_kmajor_desc(smem_u32(stage_w(s)));
+                    const uint64_t bd = sw128_kmajor_desc(smem_u32(stage_x(s)));
+                    bool ok = true;
+                    for (int k4 = 0; k4 < 4; k4++) {       // D buffer k4 holds block 4i+k4
+                        if (!wait_or_flag(&tempty[k4], (i & 1) ^ 1, a.status, abort)) {
+                            ok = false;
+                            break;
+                        }
+                        tc_fence_after();
+                        mma_i8(tmem + k4 * BN, ad + 2 * k4, bd + 2 * k4, idesc, 0);   // D_b overwrites
+                        tc_commit(&tfull[k4]);
+                    }
+                    if (!ok) break;
+                    tc_commit(&empty[s]);
+                }
+                tc_commit(done);
+            }
         }
     } else {
+        if (C::REG_SPLIT) setmaxnreg_inc<C::REGS_EPI>();
         // epilogue
         const int q = warp & 3;                 // TMEM lane quarter this warp may access
-        const int half = (warp - 2) >> 2;       // column group
+        const int half = (warp - C::EPI_WARP0) >> 2;   // column group
         const int nl = q * 32 + lane;           // row of the tile
         const int n = n0 + nl;
         const int nc = min(n, a.N - 1);
@@ -312,66 +324,63 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
         if ((kb0 & ~7) + 8 < nbt)
             sc_nxt = __ldg(reinterpret_cast<const uint4*>(srow + ((kb0 & ~7) + 8) * 2));
         const uint32_t tq = tmem + ((uint32_t)(q * 32) << 16) + half * CW;
-        for (int i = 0; i < nst; i++) {
-            const int s = i % S, u = i / S;
+        // One TMEM load (32 columns) and one wait per block; the buffer goes
+        // back to the MMA issuer as soon as it is in registers, before the
+        // rescale.  D_b arrives as a plain int32: the integer add of the bits
+        // of 1.5*2^23 (ALU pipe) gives the float 1.5*2^23 + D_b, exact for
+        // |D_b| < 2^22.  Waits are warp-uniform: the TMEM accesses are .sync.aligned.
+        uint32_t r[CW];
+        bool ok = nst > 0 && __all_sync(0xffffffffu, wait_or_flag(&full[0], 0, a.status, abort));
+        for (int i = 0; ok && i < nst; i++) {
+            const int s = i % S;
             const int kbase = kb0 + 4 * i;                 // multiple of 4
-            // waits are made warp-uniform: the TMEM accesses below are .sync.aligned
-            if (!__all_sync(0xffffffffu, wait_or_flag(&full[s], u & 1, a.status, abort))) break;
-            if (i > 0 && (kbase & 7) == 0) {
-                sc_cur = sc_nxt;
-                if (kbase + 8 < nbt)
-                    sc_nxt = __ldg(reinterpret_cast<const uint4*>(srow + (kbase + 8) * 2));
+            if (i > 0) {
+                if (!__all_sync(0xffffffffu, wait_or_flag(&full[s], (i / S) & 1, a.status, abort))) break;
+                if ((kbase & 7) == 0) {
+                    sc_cur = sc_nxt;
+                    if (kbase + 8 < nbt)
+                        sc_nxt = __ldg(reinterpret_cast<const uint4*>(srow + (kbase + 8) * 2));
+                }
             }
             const uint32_t w01 = (kbase & 4) ? sc_cur.z : sc_cur.x;
             const uint32_t w23 = (kbase & 4) ? sc_cur.w : sc_cur.y;
             const float* dxs = stage_d(s) + half * CW;
-            bool ok = true;
 #pragma unroll 1
             for (int k4 = 0; k4 < 4; k4++) {              // block kbase + k4 is in D buffer k4
-                const uint32_t wsel = ((k4 & 2) ? w23 : w01) >> ((k4 & 1) * 16);
-                const float dw = __half2float(__ushort_as_half((unsigned short)(wsel & 0xFFFFu)));
-                const float ncw = -kMagic * dw;
-                const float2 dw2 = make_float2(dw, dw), ncw2 = make_float2(ncw, ncw);
                 if (!__all_sync(0xffffffffu, wait_or_flag(&tfull[k4], i & 1, a.status, abort))) {
                     ok = false;
                     break;
                 }
                 tc_fence_after();
+                tmem_ld32(tq + k4 * BN, r);
+                const uint32_t wsel = ((k4 & 2) ? w23 : w01) >> ((k4 & 1) * 16);
+                const float dw = __half2float(__ushort_as_half((unsigned short)(wsel & 0xFFFFu)));
+                const float ncw = -kMagic * dw;
+                const float2 dw2 = make_float2(dw, dw), ncw2 = make_float2(ncw, ncw);
+                const float* dxb = dxs + k4 * BN;
+                tmem_wait_ld32(r);
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&tempty[k4]);   // buffer k4 free for block kbase + k4 + 4
+                if (DOTS && n < a.N) {
+                    const int nb = a.K / QK;
 #pragma unroll
-                for (int c = 0; c < 2; c++) {
-                    uint32_t cur[16];
-                    tmem_ld16(tq + k4 * BN + c * 16, cur);
-                    tmem_wait_ld16(cur);
-                    if (c == 1) {
-                        // re-arm the buffer for the MMA of block kbase + k4 + 4
-                        tmem_st16_const(tq + k4 * BN, kMagicBits);
-                        tmem_st16_const(tq + k4 * BN + 16, kMagicBits);
-                        tmem_wait_st();
-                        tc_fence_before();
-                        __syncwarp();
-                        if (lane == 0) mbar_arrive(&tempty[k4]);
+                    for (int j = 0; j < CW; j++) {
+                        const int m = m0 + half * CW + j;
+                        if (m < a.M) a.dots[((int64_t)m * a.N + n) * nb + kbase + k4] = (int32_t)r[j];
                     }
+                }
 #pragma unroll
-                    for (int j = 0; j < 16; j += 4) {
-                        const float4 d4 = *reinterpret_cast<const float4*>(dxs + k4 * BN + c * 16 + j);
-                        const int jj = (c * 16 + j) / 2;
-                        const float2 t0 = ffma2(make_float2(__uint_as_float(cur[j]), __uint_as_float(cur[j + 1])),
-                                                dw2, ncw2);
-                        const float2 t1 = ffma2(make_float2(__uint_as_float(cur[j + 2]), __uint_as_float(cur[j + 3])),
-                                                dw2, ncw2);
-                        acc[jj] = ffma2(t0, make_float2(d4.x, d4.y), acc[jj]);
-                        acc[jj + 1] = ffma2(t1, make_float2(d4.z, d4.w), acc[jj + 1]);
-                    }
-                    if (DOTS && n < a.N) {
-                        const int nb = a.K / QK;
-#pragma unroll
-                        for (int j = 0; j < 16; j++) {
-                            const int m = m0 + half * CW + c * 16 + j;
-                            if (m < a.M)
-                                a.dots[((int64_t)m * a.N + n) * nb + kbase + k4] =
-                                    (int32_t)(cur[j] - kMagicBits);
-                        }
-                    }
+                for (int j = 0; j < CW; j += 4) {
+                    const float4 d4 = *reinterpret_cast<const float4*>(dxb + j);
+                    const float2 t0 = ffma2(make_float2(__uint_as_float(r[j] + kMagicBits),
+                                                        __uint_as_float(r[j + 1] + kMagicBits)),
+                                            dw2, ncw2);
+                    const float2 t1 = ffma2(make_float2(__uint_as_float(r[j + 2] + kMagicBits),
+                                                        __uint_as_float(r[j + 3] + kMagicBits)),
+                                            dw2, ncw2);
+                    acc[j / 2] = ffma2(t0, make_float2(d4.x, d4.y), acc[j / 2]);
+                    acc[j / 2 + 1] = ffma2(t1, make_float2(d4.z, d4.w), acc[j / 2 + 1]);
                 }
             }
             if (!ok) break;
@@ -403,7 +412,7 @@ __global__ void __launch_bounds__(MmaCfg<BN>::THREADS, MmaCfg<BN>::CTAS_PER_SM)
             }
             __threadfence();
             asm volatile("bar.sync 1, %0;" ::"n"(EW * 32) : "memory");
-            if (warp == 2 && lane == 0) {
+            if (warp == C::EPI_WARP0 && lane == 0) {
                 int* c = a.counters + blockIdx.y * gridDim.x + blockIdx.x;
                 const int last = atomicAdd(c, 1) == splits - 1;
                 if (last) *c = 0;
