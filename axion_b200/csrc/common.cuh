@@ -153,18 +153,10 @@ __device__ inline float warp_max(float v) {
     return v;
 }
 
-// Round half away from zero and clamp to the symmetric int8 range; the
-// activation quantizer's rounding rule (C99 roundf semantics).
-// Packed fp32 fused multiply-add (sm_100): d = a * b + c per lane of the pair,
-// each rounded to nearest like fmaf, at one instruction for both.
-__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{\n\t.reg .b64 ra, rb, rc, rd;\n\tmov.b64 ra, {%2, %3};\n\tmov.b64 rb, {%4, %5};\n\t"
-        "mov.b64 rc, {%6, %7};\n\tfma.rn.f32x2 rd, ra, rb, rc;\n\tmov.b64 {%0, %1}, rd;\n\t}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
+// Packed fp32 fused multiply-add (sm_100 fma.rn.f32x2): d = a * b + c per lane
+// of the pair, each rounded to nearest like fmaf, at one instruction for both.
+// The builtin keeps the pair in a 64-bit register pair for the compiler.
+__device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) { return __ffma2_rn(a, b, c); }
 
 // Loads of data that another kernel of the same stream produced.  Kernels here
 // are launched with programmatic dependent launch: a kernel starts while its
@@ -182,6 +174,8 @@ __device__ __forceinline__ float4 ld_cg4(const float* p) {
     return __ldcg(reinterpret_cast<const float4*>(p));
 }
 
+// Round half away from zero and clamp to the symmetric int8 range; the
+// activation quantizer's rounding rule (C99 roundf semantics).
 __device__ inline int q8_round(float v) {
     float r = roundf(v);
     r = fminf(fmaxf(r, -127.0f), 127.0f);

@@ -116,35 +116,42 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
     const int nkb = a.K / 32;
     const int nch = (nkb + kMmqChunkKb - 1) / kMmqChunkKb;
     const int ch0 = blockIdx.y * a.chunks_per_split, ch1 = min(nch, ch0 + a.chunks_per_split);
+    // Copy assignment, fixed over the chunks: thread -> 16-byte piece cpc of
+    // rows cr + 32q.  kSwz(cr + 32q) == kSwz(cr), so the swizzled piece offset
+    // is one per thread, and the rows' global addresses are computed once and
+    // advance by 128 bytes per chunk.
+    const int cr = threadIdx.x >> 3, cpc = threadIdx.x & 7;
+    const int cpiece = (cpc ^ kSwz(cr)) << 4;
+    const uint8_t* wsrc[kMmqRows / 32];
+#pragma unroll
+    for (int q = 0; q < kMmqRows / 32; q++)
+        wsrc[q] = a.rows + (int64_t)min(nbase + cr + 32 * q, a.N - 1) * a.row_stride + cpc * 16;
+    // 4 fp16 scales per row (the row's scale area is padded to 16 bytes): thread r < 128
+    const uint8_t* wssrc = a.rows + (int64_t)min(nbase + (int)threadIdx.x, a.N - 1) * a.row_stride + a.K;
     // weights (and their scales) of chunk ch into stage st
     auto issue_w = [&](int ch, int st) {
-        uint8_t* W = smem + st * SM::STAGE + SM::W;
-        for (int i = threadIdx.x; i < kMmqRows * 8; i += blockDim.x) {
-            const int r = i >> 3, pc = i & 7;
-            const int64_t n = min(nbase + r, a.N - 1);
-            const int kbyte = ch * kMmqChunkKb * 32 + pc * 16;
-            const bool ok = kbyte < a.K;
-            cp_async16_zfill(W + r * 128 + ((pc ^ kSwz(r)) << 4),
-                             a.rows + n * a.row_stride + (ok ? kbyte : 0), ok);
-        }
-        // 4 fp16 scales per row; the row's scale area is padded to 16 bytes
-        uint8_t* WS = smem + st * SM::STAGE + SM::WS;
-        for (int r = threadIdx.x; r < kMmqRows; r += blockDim.x) {
-            const int64_t n = min(nbase + r, a.N - 1);
-            cp_async8(WS + r * 8, a.rows + n * a.row_stride + a.K + ch * kMmqChunkKb * 2);
-        }
+        uint8_t* W = smem + st * SM::STAGE + SM::W + cr * 128 + cpiece;
+        const bool ok = ch * kMmqChunkKb * 32 + cpc * 16 < a.K;   // a partial last chunk
+        const int koff = ok ? ch * kMmqChunkKb * 32 : -cpc * 16;  // zero fill: the row's start
+#pragma unroll
+        for (int q = 0; q < kMmqRows / 32; q++) cp_async16_zfill(W + q * 32 * 128, wsrc[q] + koff, ok);
+        if (threadIdx.x < kMmqRows)
+            cp_async8(smem + st * SM::STAGE + SM::WS + threadIdx.x * 8, wssrc + ch * kMmqChunkKb * 2);
     };
     // activation rows and scales of chunk ch into stage st
     auto issue_x = [&](int ch, int st) {
-        uint8_t* X = smem + st * SM::STAGE + SM::X;
-        float* DX = reinterpret_cast<float*>(smem + st * SM::STAGE + SM::DX);
-        for (int i = threadIdx.x; i < MR * 8; i += blockDim.x) {
-            const int r = i >> 3, c = i & 7;
-            const int64_t k = (int64_t)ch * kMmqChunkKb * 32 + c * 16;
-            const bool ok = r < a.M && k < a.K;
-            cp_async16_zfill(X + r * 128 + ((c ^ kSwz(r)) << 4), a.xq + (ok ? (int64_t)r * a.K + k : 0), ok);
+        uint8_t* X = smem + st * SM::STAGE + SM::X + cr * 128 + cpiece;
+        const int64_t k = (int64_t)ch * kMmqChunkKb * 32 + cpc * 16;
+#pragma unroll
+        for (int q = 0; q < (MR + 31) / 32; q++) {
+            const int r = cr + 32 * q;
+            if (r < MR) {
+                const bool ok = r < a.M && k < a.K;
+                cp_async16_zfill(X + q * 32 * 128, a.xq + (ok ? (int64_t)r * a.K + k : 0), ok);
+            }
         }
         // scales: 4 blocks x MR rows, 16 bytes = 4 rows per copy
+        float* DX = reinterpret_cast<float*>(smem + st * SM::STAGE + SM::DX);
         for (int i = threadIdx.x; i < kMmqChunkKb * MR / 4; i += blockDim.x) {
             const int k4 = i / (MR / 4), r4 = (i % (MR / 4)) * 4;
             const int kb = ch * kMmqChunkKb + k4;
@@ -165,6 +172,7 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
         cp_async_commit();   // group s (group 0 also holds the early weights)
     }
     const int ra = warp * 16 + g, rb = ra + 8;   // this lane's rows in the tile; both & 3 == g & 3
+    const int lane_off = (t >> 1) * 16 + (t & 1) * 8;   // byte 8t of a block, within its piece pair
     for (int ch = ch0; ch < ch1; ch++) {
         const int i = ch - ch0;
         cp_async_wait_group<NST - 2>();   // chunk ch has landed
@@ -175,17 +183,18 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
         }
         cp_async_commit();
         const uint8_t* st = smem + (i % NST) * SM::STAGE;
-        const uint8_t* W = st + SM::W;
-        const uint8_t* X = st + SM::X;
-        const float* DX = reinterpret_cast<const float*>(st + SM::DX);
+        const uint8_t* Wl = st + SM::W + ra * 128 + lane_off;   // + the block's piece offset
+        const uint8_t* Xl = st + SM::X + g * 128 + lane_off;    // + the block's piece offset + 1024 j
+        const float* DXl = reinterpret_cast<const float*>(st + SM::DX) + 2 * t;
         const uint2 sa = *reinterpret_cast<const uint2*>(st + SM::WS + ra * 8);
         const uint2 sb = *reinterpret_cast<const uint2*>(st + SM::WS + rb * 8);
 #pragma unroll
         for (int k4 = 0; k4 < kMmqChunkKb; k4++) {
-            // the 16-byte piece holding bytes 8t..8t+7 of block k4, and the half of it
-            const int c16 = (k4 * 32 + 8 * t) >> 4, c8 = (8 * t) & 15;
-            const uint2 A0 = *reinterpret_cast<const uint2*>(W + ra * 128 + ((c16 ^ kSwz(g)) << 4) + c8);
-            const uint2 A1 = *reinterpret_cast<const uint2*>(W + rb * 128 + ((c16 ^ kSwz(g)) << 4) + c8);
+            // bytes 8t..8t+7 of block k4 sit in 16-byte piece 2 k4 + t/2 of the row,
+            // stored at piece (2 k4 + t/2) ^ kSwz(g) = (2 k4 ^ kSwz(g)) + t/2
+            const int poff = ((2 * k4) ^ kSwz(g)) << 4;
+            const uint2 A0 = *reinterpret_cast<const uint2*>(Wl + poff);
+            const uint2 A1 = *reinterpret_cast<const uint2*>(Wl + poff + 8 * 128);
             const uint32_t af[4] = {A0.x, A1.x, A0.y, A1.y};
             const uint32_t swa = (k4 < 2 ? sa.x : sa.y) >> ((k4 & 1) * 16);
             const uint32_t swb = (k4 < 2 ? sb.x : sb.y) >> ((k4 & 1) * 16);
@@ -194,9 +203,9 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
             const float nca = -kMagicF * dwa, ncb = -kMagicF * dwb;
 #pragma unroll
             for (int j = 0; j < MT8; j++) {
-                const int r = 8 * j + g;
-                const uint2 B = *reinterpret_cast<const uint2*>(X + r * 128 + ((c16 ^ kSwz(r)) << 4) + c8);
-                const float2 dxv = *reinterpret_cast<const float2*>(DX + k4 * MR + 8 * j + 2 * t);
+                // activation row 8j + g: kSwz(8j + g) == kSwz(g)
+                const uint2 B = *reinterpret_cast<const uint2*>(Xl + poff + j * 8 * 128);
+                const float2 dxv = *reinterpret_cast<const float2*>(DXl + k4 * MR + 8 * j);
                 int d[4];
                 mma_s8_16832(d, af, B.x, B.y, (int)kMagicBitsI);
                 const float2 ta = ffma2(make_float2(__int_as_float(d[0]), __int_as_float(d[1])),
