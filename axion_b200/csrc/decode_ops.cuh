@@ -446,6 +446,56 @@ __device__ __forceinline__ void split_pair(float x, float y, uint32_t& hi, uint3
     lo = (uint32_t)__half_as_ushort(xl) | ((uint32_t)__half_as_ushort(yl) << 16);
 }
 
+// The CTA's merge of its warps' states and, in the last split CTA of a
+// (sequence, KV head), of the splits.  Warp w left in shared memory (at
+// w * (16 HD + 32) floats) its unnormalised O rows [16][HD] (row = head of
+// the group), then 16 running maxima and 16 sums; rows >= G are unused.
+template <int HD, bool Q8>
+__device__ __forceinline__ void attn_tc_merge(const uint8_t* tc_sm, int G, int n_heads, int n_kv,
+                                              int kvh, int m, int s, int nsplit, float* __restrict__ part,
+                                              int* __restrict__ counters, float* __restrict__ out,
+                                              int8_t* __restrict__ xq, float* __restrict__ dx, int dxt,
+                                              int warp, int lane) {
+    constexpr int W = kAttnTcWarps;
+    __syncthreads();
+    const float* m0p = reinterpret_cast<const float*>(tc_sm);
+    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
+        const int row = idx / HD, d = idx % HD;
+        float mx = -CUDART_INF_F;
+#pragma unroll
+        for (int w = 0; w < W; w++) mx = fmaxf(mx, m0p[(size_t)w * (16 * HD + 32) + 16 * HD + row]);
+        float acc = 0.0f, l = 0.0f;
+#pragma unroll
+        for (int w = 0; w < W; w++) {
+            const float* base = m0p + (size_t)w * (16 * HD + 32);
+            const float mwv = base[16 * HD + row];
+            const float f = mwv == -CUDART_INF_F ? 0.0f : expf(mwv - mx);
+            acc = fmaf(base[row * HD + d], f, acc);
+            l = fmaf(base[16 * HD + 16 + row], f, l);
+        }
+        const int h = kvh * G + row;
+        float* op = part + (((int64_t)m * n_heads + h) * nsplit + s) * (HD + 2);
+        op[d] = acc;
+        if (d == 0) {
+            op[HD] = mx;
+            op[HD + 1] = l;
+        }
+    }
+    __threadfence();
+    __syncthreads();
+    __shared__ int last;
+    if (threadIdx.x == 0) {
+        int* c = counters + m * n_kv + kvh;
+        last = atomicAdd(c, 1) == nsplit - 1;
+        if (last) *c = 0;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int hh = warp; hh < G; hh += W)
+        attn_merge_head<HD, Q8>(part, m, n_heads, kvh * G + hh, nsplit, out, xq, dx, dxt, lane);
+}
+
 template <int HD, bool Q8>
 __global__ void __launch_bounds__(kAttnTcWarps * 32)
     attn_tc_kernel(const float* __restrict__ qkv, int ldq, const int* __restrict__ pos,
@@ -627,43 +677,218 @@ __global__ void __launch_bounds__(kAttnTcWarps * 32)
         mw[16 * HD + 16 + g] = lrun[0];
         mw[16 * HD + 16 + g + 8] = lrun[1];
     }
-    __syncthreads();
-    const float* m0p = reinterpret_cast<const float*>(tc_sm);
-    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
-        const int row = idx / HD, d = idx % HD;
-        float mx = -CUDART_INF_F;
+    attn_tc_merge<HD, Q8>(tc_sm, G, n_heads, n_kv, kvh, m, s, nsplit, part, counters, out, xq, dx,
+                          dxt, warp, lane);
+}
+
+// Transposed tensor-core attention for query groups of at most 8 heads (the
+// Llama-3 and TinyLlama groups: 4 and 8).  The 16 tokens of a page are the
+// MMA rows and the heads the 8 columns, so no MMA row is padding:
+//   S^T [16 tokens x 8 heads] = K Q^T   (A = K page rows by ldmatrix, B = Q^T in registers)
+//   O^T [HD x 8 heads] += V^T P^T        (A = V^T by ldmatrix.trans, B = P^T)
+// P^T's B fragments come from the S^T accumulators by one register transpose
+// (movmatrix) per 8x8 block.  Q and P keep the fp16 high + residual split of
+// the kernel above (fp32 accuracy); half the MMAs of the 16-head layout and
+// half the output registers.  Grid, shared memory, splits and merge as above.
+constexpr int kAttnTctBufs = 3;   // page buffers per warp: two pages in flight ahead
+template <int HD>
+struct AttnTctSmem {
+    static constexpr size_t STAGE = (size_t)kAttnTcWarps * kAttnTctBufs * 2 /*K,V*/ * 16 * HD * 2;
+    static constexpr size_t MERGE = AttnTcSmem<HD>::MERGE;
+    static constexpr size_t PG = STAGE > MERGE ? STAGE : MERGE;   // offset of the page ids
+};
+template <int HD>
+inline size_t attn_tct_smem_bytes(int bps) {
+    return AttnTctSmem<HD>::PG + ((size_t)bps * sizeof(int) + 15) / 16 * 16;
+}
+
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t a) {
+    uint32_t d;
+    asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+    return d;
+}
+
+template <int HD, bool Q8>
+__global__ void __launch_bounds__(kAttnTcWarps * 32)
+    attn_tct_kernel(const float* __restrict__ qkv, int ldq, const int* __restrict__ pos,
+                    const __half* __restrict__ kc, const __half* __restrict__ vc,
+                    const int* __restrict__ block_table, int max_blocks, int n_heads, int n_kv,
+                    int G, int bps, float scale, float* __restrict__ part, int* __restrict__ counters,
+                    float* __restrict__ out, int8_t* __restrict__ xq, float* __restrict__ dx, int dxt) {
+    constexpr int B = 16;
+    constexpr int W = kAttnTcWarps;
+    constexpr int KS = HD / 16;              // k-steps of the score product
+    constexpr int MT = HD / 16;              // 16-dim row tiles of O^T
+    constexpr int CH = HD / 8;               // 16-byte chunks per row
+    constexpr int PAGE = B * HD;             // halves per K (or V) page
+    extern __shared__ __align__(16) uint8_t tc_sm[];
+    constexpr int NBUF = kAttnTctBufs;
+    __half* stage = reinterpret_cast<__half*>(tc_sm);   // [W][NBUF][K,V][B][HD]
+    int* pg = reinterpret_cast<int*>(tc_sm + AttnTctSmem<HD>::PG);
+    const int kvh = blockIdx.x, m = blockIdx.y, s = blockIdx.z, nsplit = gridDim.z;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int g = lane >> 2, t = lane & 3;
+    const int b0 = s * bps;
+    for (int i = threadIdx.x; i < bps; i += blockDim.x)
+        pg[i] = b0 + i < max_blocks ? block_table[m * max_blocks + b0 + i] : 0;
+    pdl_launch_dependents();
+    pdl_wait();
+    const int ctx = min(ld_cg(pos + m) + 1, max_blocks * B);
+    const int nblk = (ctx + B - 1) / B;
+    const int b1 = min(nblk, b0 + bps);
+    __syncthreads();   // pg visible
+    // Q^T fragments (B operand, column = head g of the group, zero for g >= G):
+    // [k][0] dims 16k + 2t (+1), [k][1] dims 16k + 8 + 2t (+1); fp16 high and residual
+    uint32_t qh[KS][2], ql[KS][2];
+    {
+        const float* q0 = qkv + (int64_t)m * ldq + (int64_t)(kvh * G) * HD;
 #pragma unroll
-        for (int w = 0; w < W; w++) mx = fmaxf(mx, m0p[(size_t)w * (16 * HD + 32) + 16 * HD + row]);
-        float acc = 0.0f, l = 0.0f;
+        for (int k = 0; k < KS; k++) {
 #pragma unroll
-        for (int w = 0; w < W; w++) {
-            const float* base = m0p + (size_t)w * (16 * HD + 32);
-            const float mwv = base[16 * HD + row];
-            const float f = mwv == -CUDART_INF_F ? 0.0f : expf(mwv - mx);
-            acc = fmaf(base[row * HD + d], f, acc);
-            l = fmaf(base[16 * HD + 16 + row], f, l);
-        }
-        const int h = kvh * G + row;
-        float* op = part + (((int64_t)m * n_heads + h) * nsplit + s) * (HD + 2);
-        op[d] = acc;
-        if (d == 0) {
-            op[HD] = mx;
-            op[HD + 1] = l;
+            for (int r = 0; r < 2; r++) {
+                float x = 0.0f, y = 0.0f;
+                if (g < G) {
+                    const float2 v = ld_cg2(q0 + (int64_t)g * HD + k * 16 + 8 * r + 2 * t);
+                    x = v.x;
+                    y = v.y;
+                }
+                split_pair(x, y, qh[k][r], ql[k][r]);
+            }
         }
     }
-    __threadfence();
-    __syncthreads();
-    __shared__ int last;
-    if (threadIdx.x == 0) {
-        int* c = counters + m * n_kv + kvh;
-        last = atomicAdd(c, 1) == nsplit - 1;
-        if (last) *c = 0;
+    // O^T tile mt: [0] dim 16 mt + g, head 2t; [1] head 2t + 1; [2], [3] dim + 8
+    float o[MT][4];
+#pragma unroll
+    for (int n = 0; n < MT; n++) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.0f;
+    float mrun[2] = {-CUDART_INF_F, -CUDART_INF_F}, lrun[2] = {0.0f, 0.0f};   // heads 2t, 2t + 1
+    __half* wst = stage + (size_t)warp * NBUF * 2 * PAGE;
+    const uint32_t wst_s = smem_u32(wst);
+    const int npw = b1 > b0 + warp ? (b1 - b0 - warp + W - 1) / W : 0;
+    auto issue = [&](int i) {            // page number i of this warp -> buffer i % NBUF
+        const int blk = b0 + warp + i * W;
+        const int64_t off = ((int64_t)pg[blk - b0] * n_kv + kvh) * PAGE;
+        __half* kb = wst + (size_t)(i % NBUF) * 2 * PAGE;
+        __half* vb = kb + PAGE;
+#pragma unroll
+        for (int c = lane; c < B * CH; c += 32) {
+            const int r = c / CH, ch = c % CH;
+            const int sw = r * HD + ((ch ^ (r & 7)) * 8);
+            cp_async16(kb + sw, kc + off + r * HD + ch * 8);
+            cp_async16(vb + sw, vc + off + r * HD + ch * 8);
+        }
+    };
+    // NBUF - 1 pages ahead: page i + NBUF - 1 is requested while page i is used
+    static_assert(NBUF == 3, "wait counts below");
+    for (int i = 0; i < NBUF - 1; i++) {
+        if (i < npw) issue(i);
+        cp_async_commit();
     }
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
-    for (int hh = warp; hh < G; hh += W)
-        attn_merge_head<HD, Q8>(part, m, n_heads, kvh * G + hh, nsplit, out, xq, dx, dxt, lane);
+    const int mi = lane >> 3, rr = lane & 7;
+    for (int i = 0; i < npw; i++) {
+        if (i + NBUF - 1 < npw) issue(i + NBUF - 1);
+        cp_async_commit();                 // (possibly empty) group of page i + NBUF - 1
+        cp_async_wait_group<NBUF - 1>();   // page i has landed
+        __syncwarp();
+        const int blk = b0 + warp + i * W;
+        const uint32_t kb = wst_s + (uint32_t)((i % NBUF) * 2 * PAGE * 2);
+        const uint32_t vb = kb + PAGE * 2;
+        // S^T = K Q^T.  A fragment of K for k-step k: matrices (tokens 0-7 | 8-15) x
+        // (dims 16k..+7 | 16k+8..+15), lane l addressing row l % 8 of matrix l / 8
+        float sc[4] = {0.0f, 0.0f, 0.0f, 0.0f};   // tok g: heads 2t, 2t+1; tok g + 8: same
+        {
+            const int tok = rr + ((mi & 1) << 3);
+#pragma unroll
+            for (int k = 0; k < KS; k++) {
+                const int ch = k * 2 + (mi >> 1);
+                uint32_t kf[4];
+                ldsm_x4(kf, kb + (uint32_t)((tok * HD + ((ch ^ (tok & 7)) * 8)) * 2));
+                mma_f16_16816(sc, kf, qh[k][0], qh[k][1]);
+                mma_f16_16816(sc, kf, ql[k][0], ql[k][1]);
+            }
+        }
+        // online softmax per head column (2t + hh): tokens g, g + 8 of this lane,
+        // the other tokens across the 8 lanes of the same t
+        float p[4];
+#pragma unroll
+        for (int hh = 0; hh < 2; hh++) {
+            float mt = -CUDART_INF_F;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const int tok = blk * B + g + 8 * j;
+                float& v = sc[2 * j + hh];
+                v = tok < ctx ? __fmul_rn(v, scale) : -CUDART_INF_F;
+                mt = fmaxf(mt, v);
+            }
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 4));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 8));
+            mt = fmaxf(mt, __shfl_xor_sync(0xffffffffu, mt, 16));
+            const float mnew = fmaxf(mrun[hh], mt);
+            const float corr = expf(mrun[hh] - mnew);   // 0 when mrun is -inf
+            float ps = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 2; j++) {
+                const float v = sc[2 * j + hh];
+                const float e = v == -CUDART_INF_F ? 0.0f : expf(v - mnew);
+                p[2 * j + hh] = e;
+                ps += e;
+            }
+            lrun[hh] = fmaf(lrun[hh], corr, ps);
+            mrun[hh] = mnew;
+#pragma unroll
+            for (int n = 0; n < MT; n++) {
+                o[n][hh] *= corr;
+                o[n][2 + hh] *= corr;
+            }
+        }
+        // P^T fragments (B operand: k = tokens, n = head g) by transposing the
+        // 8x8 blocks (tokens 0-7, 8-15) x heads held in the S^T layout
+        uint32_t h01, l01, h23, l23;
+        split_pair(p[0], p[1], h01, l01);   // token g, heads 2t, 2t+1
+        split_pair(p[2], p[3], h23, l23);   // token g + 8
+        const uint32_t pbh0 = movmatrix_t(h01), pbh1 = movmatrix_t(h23);
+        const uint32_t pbl0 = movmatrix_t(l01), pbl1 = movmatrix_t(l23);
+        // O^T += V^T P^T.  A fragment of V^T for row tile mt: matrices (dims 16mt..+7 |
+        // +8..+15) x (tokens 0-7 | 8-15), each the transpose of a stored 8x8 block
+        {
+            const int tok = rr + ((mi >> 1) << 3);
+#pragma unroll
+            for (int mt = 0; mt < MT; mt++) {
+                const int ch = mt * 2 + (mi & 1);
+                uint32_t vf[4];
+                ldsm_x4_t(vf, vb + (uint32_t)((tok * HD + ((ch ^ (tok & 7)) * 8)) * 2));
+                mma_f16_16816(o[mt], vf, pbh0, pbh1);
+                mma_f16_16816(o[mt], vf, pbl0, pbl1);
+            }
+        }
+        __syncwarp();   // buffer i % NBUF free for page i + NBUF
+    }
+    cp_async_wait_all();
+    // column sums over the 8 lanes of the same t
+#pragma unroll
+    for (int hh = 0; hh < 2; hh++) {
+        lrun[hh] += __shfl_xor_sync(0xffffffffu, lrun[hh], 4);
+        lrun[hh] += __shfl_xor_sync(0xffffffffu, lrun[hh], 8);
+        lrun[hh] += __shfl_xor_sync(0xffffffffu, lrun[hh], 16);
+    }
+    // the warp's state in the merge layout: rows = heads, [16][HD], then m, l
+    __syncthreads();   // every warp is done with the staging buffers
+    float* mw = reinterpret_cast<float*>(tc_sm) + (size_t)warp * (16 * HD + 32);
+#pragma unroll
+    for (int n = 0; n < MT; n++) {
+        const int d = n * 16 + g;
+        mw[(2 * t) * HD + d] = o[n][0];
+        mw[(2 * t + 1) * HD + d] = o[n][1];
+        mw[(2 * t) * HD + d + 8] = o[n][2];
+        mw[(2 * t + 1) * HD + d + 8] = o[n][3];
+    }
+    if (g == 0) {
+        mw[16 * HD + 2 * t] = mrun[0];
+        mw[16 * HD + 2 * t + 1] = mrun[1];
+        mw[16 * HD + 16 + 2 * t] = lrun[0];
+        mw[16 * HD + 16 + 2 * t + 1] = lrun[1];
+    }
+    attn_tc_merge<HD, Q8>(tc_sm, G, n_heads, n_kv, kvh, m, s, nsplit, part, counters, out, xq, dx,
+                          dxt, warp, lane);
 }
 
 // ---- RoPE + KV append over product rows (wide batches, prefill chunks) ----------

@@ -427,19 +427,22 @@ int launch_attention(axdec_model* m, int M, int layer, cudaStream_t s, int dxt) 
         // fp16 pages, head dim 64 / 128, batches: the tensor-core kernel (one
         // sequence with short splits keeps the scalar kernel, whose single
         // pass has less set-up per CTA)
-        const size_t smem = attn_tc_smem_bytes<HD>(m->bps);
         const bool q8 = c.act_mode != AXQ8_ACT_F32;
-        auto kern = q8 ? attn_tc_kernel<HD, true> : attn_tc_kernel<HD, false>;
-        static int configured[2][64] = {{0}};
+        // groups of at most 8 heads: tokens as the MMA rows (no padding rows)
+        const bool tr = G <= 8;
+        const size_t smem = tr ? attn_tct_smem_bytes<HD>(m->bps) : attn_tc_smem_bytes<HD>(m->bps);
+        auto kern = tr ? (q8 ? attn_tct_kernel<HD, true> : attn_tct_kernel<HD, false>)
+                       : (q8 ? attn_tc_kernel<HD, true> : attn_tc_kernel<HD, false>);
+        static int configured[2][2][64] = {{{0}}};
         const int dev = m->ds->device < 64 ? m->ds->device : 63;
         constexpr int kMaxSmem = 200 * 1024;
         if (smem > (size_t)kMaxSmem)
             return fail(AXQ8_ERR_UNSUPPORTED, "attention: %zu B of shared memory", smem);
-        if (smem > 48 * 1024 && !configured[q8][dev]) {
+        if (smem > 48 * 1024 && !configured[tr][q8][dev]) {
             AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                kMaxSmem),
                           "attention smem attribute");
-            configured[q8][dev] = 1;
+            configured[tr][q8][dev] = 1;
         }
         Layer& Ly = m->L[layer];
         const float scale = 1.0f / std::sqrt((float)HD);   // mha.cpp:250

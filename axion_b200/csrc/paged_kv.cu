@@ -79,17 +79,18 @@ int launch_attn(DeviceState* ds, const axkv_cache_t* c, const float* q, int n_se
     const float scale = 1.0f / std::sqrt((float)HD);   // mha.cpp:250
     if constexpr (std::is_same<KV, __half>::value && HD >= 64) {
         if (n_seq >= 2) {
-            const size_t smem = attn_tc_smem_bytes<HD>(bps);
-            auto kern = attn_tc_kernel<HD, false>;
+            const bool tr = G <= 8;   // groups of at most 8 heads: tokens as the MMA rows
+            const size_t smem = tr ? attn_tct_smem_bytes<HD>(bps) : attn_tc_smem_bytes<HD>(bps);
+            auto kern = tr ? attn_tct_kernel<HD, false> : attn_tc_kernel<HD, false>;
             constexpr int kMaxSmem = 200 * 1024;
             if (smem > (size_t)kMaxSmem) return fail(AXQ8_ERR_UNSUPPORTED, "attention: shared memory");
-            static int configured[64] = {0};
+            static int configured[2][64] = {{0}};
             const int dev = ds->device < 64 ? ds->device : 63;
-            if (smem > 48 * 1024 && !configured[dev]) {
+            if (smem > 48 * 1024 && !configured[tr][dev]) {
                 AXQ8_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    kMaxSmem),
                               "attention smem attribute");
-                configured[dev] = 1;
+                configured[tr][dev] = 1;
             }
             AXQ8_CUDA_TRY(launch_k(kern, dim3(c->n_kv_heads, n_seq, nsplit), dim3(kAttnTcWarps * 32),
                                    smem, s, false, q, n_heads * HD, q_pos, (const __half*)c->k_pages,
