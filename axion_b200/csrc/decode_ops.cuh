@@ -1221,9 +1221,36 @@ static __global__ void argmax_rows_kernel(const float* __restrict__ logits, int 
     const int m = blockIdx.y;
     const float* row = logits + (int64_t)m * V;
     unsigned long long best = 0ull;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < V; i += gridDim.x * blockDim.x) {
-        const unsigned long long k = argmax_key(ld_cg(row + i), i + idx_offset);
-        best = k > best ? k : best;
+    // 4 consecutive logits per load, 4 loads in flight per thread (rows of V %
+    // 4 == 0 floats start 16-byte aligned; other widths take the scalar loop)
+    const int stride = gridDim.x * blockDim.x;
+    const int i0 = blockIdx.x * blockDim.x + threadIdx.x;
+    if ((V & 3) == 0) {
+        const int V4 = V / 4;
+        for (int i = i0; i < V4; i += 4 * stride) {
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; u++)
+                v[u] = i + u * stride < V4 ? ld_cg4(row + 4 * (i + u * stride))
+                                           : make_float4(-CUDART_INF_F, -CUDART_INF_F, -CUDART_INF_F,
+                                                         -CUDART_INF_F);
+#pragma unroll
+            for (int u = 0; u < 4; u++) {
+                if (i + u * stride >= V4) break;
+                const int c = 4 * (i + u * stride) + idx_offset;
+                const unsigned long long k0 = argmax_key(v[u].x, c), k1 = argmax_key(v[u].y, c + 1);
+                const unsigned long long k2 = argmax_key(v[u].z, c + 2), k3 = argmax_key(v[u].w, c + 3);
+                best = k0 > best ? k0 : best;
+                best = k1 > best ? k1 : best;
+                best = k2 > best ? k2 : best;
+                best = k3 > best ? k3 : best;
+            }
+        }
+    } else {
+        for (int i = i0; i < V; i += stride) {
+            const unsigned long long k = argmax_key(ld_cg(row + i), i + idx_offset);
+            best = k > best ? k : best;
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -1236,7 +1263,7 @@ static __global__ void argmax_rows_kernel(const float* __restrict__ logits, int 
 // ---- greedy step advance after a cross-rank argmax ------------------------------
 // The tensor-parallel LM head (and the wide-batch argmax) leave each
 // sequence's packed (logit, global index) key in amax_key; after the max
-// all-reduce over ranks one thread performs the advance of the argmax epilogue: record the token,
+// all-reduce over ranks one thread per sequence performs the advance of the argmax epilogue: record the token,
 // feed the next input (prompt token or the argmax), move the position, and
 // zero the key for the next step.
 static __global__ void argmax_advance_kernel(unsigned long long* __restrict__ amax_key, int M,
@@ -1245,9 +1272,9 @@ static __global__ void argmax_advance_kernel(unsigned long long* __restrict__ am
                                       int* __restrict__ out_tokens, int* __restrict__ argmax_out) {
     pdl_launch_dependents();
     pdl_wait();
-    if (threadIdx.x != 0 || blockIdx.x != 0) return;
     const int n_prompt = ld_cg(ctl), feed_len = ld_cg(ctl + 1), max_out = ld_cg(ctl + 2);
-    for (int m = 0; m < M; m++) {
+    // one thread per sequence: the sequences' advances are independent
+    for (int m = blockIdx.x * blockDim.x + threadIdx.x; m < M; m += gridDim.x * blockDim.x) {
         const unsigned long long k = __ldcg(amax_key + m);
         amax_key[m] = 0ull;
         const int idx = k == 0ull ? 0 : argmax_key_index(k);

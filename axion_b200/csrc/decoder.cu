@@ -600,7 +600,7 @@ int launch_step_wide(axdec_model* m, int M, cudaStream_t s) {
                              "axdec: argmax all-reduce")))
             return rc;
     }
-    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3(1), dim3(32), 0, s, true, m->amax_key, M,
+    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3((M + 63) / 64), dim3(64), 0, s, true, m->amax_key, M,
                            m->pos, m->tokens, (const int*)m->feed, (const int*)m->ctl,
                            m->out_tokens, m->argmax),
                   "argmax advance launch");
@@ -726,7 +726,7 @@ int launch_step_kv(axdec_model* m, int M, cudaStream_t s) {
                                         m->comm, s),
                          "axdec: argmax all-reduce")))
         return rc;
-    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3(1), dim3(32), 0, s, true, m->amax_key, M,
+    AXQ8_CUDA_TRY(launch_k(argmax_advance_kernel, dim3((M + 63) / 64), dim3(64), 0, s, true, m->amax_key, M,
                            m->pos, m->tokens, (const int*)m->feed, (const int*)m->ctl,
                            m->out_tokens, m->argmax),
                   "argmax advance launch");

@@ -415,9 +415,9 @@ __device__ __forceinline__ void argmax_tail(const GemvArgs& a, const unsigned lo
         if (threadIdx.x == 0) *a.done = 0;
         return;
     }
-    if (threadIdx.x == 0) {
+    {   // one thread per sequence
         const int n_prompt = ld_cg(a.ctl), feed_len = ld_cg(a.ctl + 1), max_out = ld_cg(a.ctl + 2);
-        for (int m = 0; m < a.M; m++) {
+        for (int m = threadIdx.x; m < a.M; m += blockDim.x) {
             const unsigned long long k = atomicExch(a.amax_key + m, 0ull);
             const int idx = k == 0ull ? 0 : argmax_key_index(k);
             const int p = ld_cg(a.pos + m);
@@ -428,7 +428,7 @@ __device__ __forceinline__ void argmax_tail(const GemvArgs& a, const unsigned lo
             a.tokens[m] = np < feed_len ? ld_cg(a.feed + m * feed_len + np) : idx;
             a.pos[m] = np;
         }
-        *a.done = 0;
+        if (threadIdx.x == 0) *a.done = 0;
     }
 }
 
