@@ -47,30 +47,6 @@ static __global__ void embed_kernel(const uint8_t* __restrict__ rows, int64_t rs
 }
 
 // ---- RMSNorm (+ A8 quantization) ------------------------------------------------
-// A8 quantization of one 32-block held by 4 consecutive lanes, 8 values each
-// (lane 4k + i holds elements 8i..8i+7): the 8 quants go to q, the scale to *d
-// from the group's first lane.  Bit-identical to quant_block_warp.  Every lane
-// of the warp calls it (full-mask shuffles); `valid` only gates the stores.
-__device__ __forceinline__ void quant_block_quad(const float (&v)[8], int lane, bool valid,
-                                                 int8_t* q, float* d) {
-    uint32_t ab = 0;
-#pragma unroll
-    for (int e = 0; e < 8; e++) ab = max(ab, __float_as_uint(fabsf(v[e])));
-    ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 1));
-    ab = max(ab, __shfl_xor_sync(0xffffffffu, ab, 2));
-    const float amax = __uint_as_float(ab);
-    const float id = amax == 0.0f ? 0.0f : __fdiv_rn(127.0f, amax);
-    uint32_t lo = 0, hi = 0;
-#pragma unroll
-    for (int e = 0; e < 4; e++) {
-        lo |= (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[e], id)) << (8 * e);
-        hi |= (uint32_t)(uint8_t)(int8_t)q8_round(__fmul_rn(v[e + 4], id)) << (8 * e);
-    }
-    if (!valid) return;
-    *reinterpret_cast<uint2*>(q) = make_uint2(lo, hi);
-    if ((lane & 3) == 0) *d = __fdiv_rn(amax, 127.0f);
-}
-
 __device__ __forceinline__ void load8(const float* p, float (&v)[8]) {
     const float4 a = *reinterpret_cast<const float4*>(p);
     const float4 b = *reinterpret_cast<const float4*>(p + 4);

@@ -107,6 +107,7 @@ struct axdec_model {
     std::map<int, Graph> graphs;  // per batch size
     // batched prefill (A8): buffers of one prompt chunk, allocated on first use
     int prefill_mode = 1;         // 1: batched where supported, 0: through the decode step
+    bool silu_fused = true;       // wide steps: SiLU*up + A8 in the gate|up skinny product
     int pre_cap = 0;              // rows the chunk buffers hold
     float* ph = nullptr;          // [cap, H] residual stream of the chunk
     int8_t* pxq = nullptr;        // [cap, maxK] A8 activations
@@ -535,16 +536,33 @@ bool use_skinny(int64_t N, int64_t K, int M) {
     return o >= 0 ? M <= o : skinny_preferred(N, M);
 }
 
-int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
-                const float* resid, float* y, cudaStream_t s) {
+axq8_weight_t wide_weight(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K) {
     axq8_weight_t w = {};
     w.rows = const_cast<uint8_t*>(rows);
     w.N = N;
     w.K = K;
     w.row_stride = q8r_row_stride(K);
     w.device = m->ds->device;
-    if (use_skinny(N, K, M)) return mmq_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, s);
-    return mma_linear(m->ds, &w, m->xq, m->dx, M, resid, y, N, nullptr, s, &m->mma_sc);
+    return w;
+}
+
+// y = x.W^T (+ resid) for the A8 activation xq / dxT (transposed scales).
+int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
+                const float* resid, float* y, const int8_t* xq, const float* dxT, cudaStream_t s) {
+    axq8_weight_t w = wide_weight(m, rows, N, K);
+    if (use_skinny(N, K, M)) return mmq_linear(m->ds, &w, xq, dxT, M, resid, y, N, s);
+    return mma_linear(m->ds, &w, xq, dxT, M, resid, y, N, nullptr, s, &m->mma_sc);
+}
+int wide_linear(axdec_model* m, const uint8_t* rows, int64_t N, int64_t K, int M,
+                const float* resid, float* y, cudaStream_t s) {
+    return wide_linear(m, rows, N, K, M, resid, y, m->xq, m->dx, s);
+}
+
+// Whether a wide step's gate|up product computes SiLU*up and its A8
+// quantization itself (the skinny product; the fp32 gate|up is never written).
+bool wide_silu_fused(axdec_model* m, int M) {
+    const int64_t N = 2 * (int64_t)m->c.ffn;
+    return m->silu_fused && N % 64 == 0 && use_skinny(N, m->c.hidden, M);
 }
 
 // Wide batches (M >= 9): every linear on the tensor cores (the skinny
@@ -579,11 +597,22 @@ int launch_step_wide(axdec_model* m, int M, cudaStream_t s) {
         if ((rc = wide_linear(m, Ly.o, H, m->Nq, M, resid, hidden_partial(m), s))) return rc;
         if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
         if ((rc = launch_rmsnorm(m, M, m->h, Ly.ffn_norm, s, dxt))) return rc;
-        if ((rc = wide_linear(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu, s))) return rc;
-        AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, silu_grid(M, F), dim3(kSiluThreads), 0, s, true,
-                               (const float*)m->gu, F, M, (float*)nullptr, m->xq, m->dx, dxt),
-                      "silu launch");
-        if ((rc = wide_linear(m, Ly.down, H, F, M, resid, hidden_partial(m), s))) return rc;
+        if (wide_silu_fused(m, M)) {
+            // SiLU*up -> A8 from the gate|up product straight into the gu
+            // buffer's storage (it must not alias the product's input xq / dx)
+            int8_t* sq = reinterpret_cast<int8_t*>(m->gu);
+            float* sdx = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(m->gu) +
+                                                  ((size_t)M * F + 255) / 256 * 256);
+            const axq8_weight_t wgu = wide_weight(m, Ly.gu, 2 * (int64_t)F, H);
+            if ((rc = mmq_linear_silu(ds, &wgu, m->xq, m->dx, M, sq, sdx, dxt, s))) return rc;
+            if ((rc = wide_linear(m, Ly.down, H, F, M, resid, hidden_partial(m), sq, sdx, s))) return rc;
+        } else {
+            if ((rc = wide_linear(m, Ly.gu, 2 * (int64_t)F, H, M, nullptr, m->gu, s))) return rc;
+            AXQ8_CUDA_TRY(launch_k(silu_mul_kernel<true>, silu_grid(M, F), dim3(kSiluThreads), 0, s, true,
+                                   (const float*)m->gu, F, M, (float*)nullptr, m->xq, m->dx, dxt),
+                          "silu launch");
+            if ((rc = wide_linear(m, Ly.down, H, F, M, resid, hidden_partial(m), s))) return rc;
+        }
         if (m->tp > 1 && (rc = allreduce_hidden(m, M, s))) return rc;
     }
     if ((rc = launch_rmsnorm(m, M, m->h, m->out_norm, s, dxt))) return rc;
@@ -1075,6 +1104,10 @@ int axdec_create(const axdec_config_t* cfg, axdec_model_t** out) {
     m->tp = tp;
     m->rank = rank;
     m->ds = ds;
+    {   // AXDEC_SILU_FUSE=0: SiLU*up as a kernel of its own in wide steps (tuning, comparisons)
+        const char* e = getenv("AXDEC_SILU_FUSE");
+        m->silu_fused = !(e && atoi(e) == 0);
+    }
     m->Nq = c.n_heads * c.head_dim;
     m->Nkv = c.n_kv_heads * c.head_dim;
     m->Nqkv = m->Nq + 2 * m->Nkv;

@@ -245,7 +245,7 @@ MmqPlan mmq_plan(DeviceState* ds, int64_t N, int64_t K, int64_t M) {
     p.splits = (nch + p.per - 1) / p.per;
     return p;
 }
-template <int MT8>
+template <int MT8, bool SILU = false>
 int mmq_launch(const MmqArgs& a, dim3 grid, cudaStream_t s) {
     constexpr int smem = MmqSmem<MT8>::BYTES;
     static bool configured[kMaxDevices] = {};
@@ -253,7 +253,7 @@ int mmq_launch(const MmqArgs& a, dim3 grid, cudaStream_t s) {
     AXQ8_CUDA_TRY(cudaGetDevice(&dev), "q8_mmq device");
     if (dev < 0 || dev >= kMaxDevices) return fail(AXQ8_ERR_INVALID, "skinny linear: device id");
     if (!configured[dev]) {   // once per device: idempotent, a repeat is harmless
-        AXQ8_CUDA_TRY(cudaFuncSetAttribute(q8_mmq_kernel<MT8>,
+        AXQ8_CUDA_TRY(cudaFuncSetAttribute(q8_mmq_kernel<MT8, SILU>,
                                            cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
                       "q8_mmq shared memory attribute");
         configured[dev] = true;
@@ -272,7 +272,7 @@ int mmq_launch(const MmqArgs& a, dim3 grid, cudaStream_t s) {
     attr[1].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = grid.y > 1 ? 2 : 1;
-    AXQ8_CUDA_TRY(cudaLaunchKernelEx(&cfg, q8_mmq_kernel<MT8>, a), "q8_mmq launch");
+    AXQ8_CUDA_TRY(cudaLaunchKernelEx(&cfg, q8_mmq_kernel<MT8, SILU>, a), "q8_mmq launch");
     return AXQ8_OK;
 }
 }  // namespace
@@ -302,6 +302,33 @@ int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const 
     if (M <= 16) return mmq_launch<2>(a, grid, stream);
     if (M <= 32) return mmq_launch<4>(a, grid, stream);
     return mmq_launch<8>(a, grid, stream);
+}
+
+int mmq_linear_silu(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
+                    int64_t M, int8_t* sq, float* sdx, int sdxt, cudaStream_t stream) {
+    if (!w || M < 1 || M > kMmqMaxM || w->K % QK || w->K > (1 << 24) || w->N > (1 << 30) ||
+        w->N % 64 || !xq || !dxT || !sq || !sdx || sdxt < 0)
+        return fail(AXQ8_ERR_INVALID, "skinny linear + SiLU: unsupported arguments");
+    const MmqPlan plan = mmq_plan(ds, w->N, w->K, M);
+    if (plan.tiles > 0x7fffffff) return fail(AXQ8_ERR_UNSUPPORTED, "skinny linear: N too large");
+    MmqArgs a = {};
+    a.rows = static_cast<const uint8_t*>(w->rows);
+    a.row_stride = w->row_stride;
+    a.N = (int)w->N;
+    a.K = (int)w->K;
+    a.M = (int)M;
+    a.xq = xq;
+    a.dxT = dxT;
+    a.Mp = (int)mma_scale_pitch(M);
+    a.chunks_per_split = plan.per;
+    a.sq = sq;
+    a.sdx = sdx;
+    a.sdxt = sdxt;
+    const dim3 grid((unsigned)plan.tiles, (unsigned)plan.splits);
+    if (M <= 8) return mmq_launch<1, true>(a, grid, stream);
+    if (M <= 16) return mmq_launch<2, true>(a, grid, stream);
+    if (M <= 32) return mmq_launch<4, true>(a, grid, stream);
+    return mmq_launch<8, true>(a, grid, stream);
 }
 
 int mma_quantize(DeviceState* ds, const float* x, int64_t M, int64_t K, int8_t* xq, float* dxT,

@@ -67,6 +67,14 @@ inline bool mma_shape_ok(int64_t N, int64_t K, int64_t M) {
 int mmq_linear(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
                int64_t M, const float* residual, float* y, int64_t ldy, cudaStream_t stream);
 
+// The skinny product of the stacked gate|up weight stored interleaved (rows
+// gate_j, up_j; N % 64 == 0) fused with SiLU*up and its A8 quantization:
+// sq [M][N/2] int8 and its block scales sdx ([b * sdxt + m] for sdxt > 0, else
+// [m * N/64 + b]); bit-identical to mmq_linear into fp32 followed by
+// silu_mul_kernel<true>.  sq / sdx must not alias xq / dxT.
+int mmq_linear_silu(DeviceState* ds, const axq8_weight_t* w, const int8_t* xq, const float* dxT,
+                    int64_t M, int8_t* sq, float* sdx, int sdxt, cudaStream_t stream);
+
 // Mp for a given M (row pitch of dxT).
 inline int64_t mma_scale_pitch(int64_t M) { return (M + 3) / 4 * 4; }
 

@@ -88,6 +88,10 @@ struct MmqArgs {
     const float* residual;   // optional [M][ldy]
     float* y;                // [M][ldy]
     int ldy;
+    // SILU launches: the rows are (gate_j, up_j) pairs; out = A8(silu(gate) * up)
+    int8_t* sq;              // [M][N/2]
+    float* sdx;              // its block scales: [b * sdxt + m] (sdxt > 0), else [m * N/64 + b]
+    int sdxt;
 };
 
 __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a, uint32_t b0, uint32_t b1,
@@ -101,7 +105,12 @@ __device__ __forceinline__ void mma_s8_16832(int* d, const uint32_t* a, uint32_t
 
 // Launched with cluster dimensions (1, gridDim.y, 1) when gridDim.y > 1, and
 // MmqSmem<MT8>::BYTES of dynamic shared memory.
-template <int MT8>   // 8-row activation tiles (M <= 8 * MT8)
+// SILU: the weight rows are the stacked gate|up weight stored interleaved
+// (gate row j, up row j), N % 64 == 0; instead of y the combine writes
+// a = silu(gate) * up, rounded per op as silu_mul_kernel does, quantized to A8
+// (quant_block_quad) into sq / sdx: the SiLU*up kernel and the fp32 gate|up
+// round trip are folded into the product.
+template <int MT8, bool SILU = false>   // 8-row activation tiles (M <= 8 * MT8)
 __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs a) {
     constexpr uint32_t kMagicBitsI = 0x4B400000u;   // 1.5 * 2^23 as fp32
     constexpr float kMagicF = 12582912.0f;
@@ -220,7 +229,7 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
     cp_async_wait_all();   // nothing of this CTA still lands in the stages
     // outputs: rows n0 + g (+8), columns 8j + 2t (+1)
     const int splits = gridDim.y;
-    if (splits == 1) {
+    if (!SILU && splits == 1) {
 #pragma unroll
         for (int j = 0; j < MT8; j++)
 #pragma unroll
@@ -234,7 +243,8 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
             }
         return;
     }
-    // split launch: partial tile -> shared memory, then the cluster's combine
+    // split launch (and every SILU launch): partial tile -> shared memory, then
+    // the cluster's combine (a single CTA combines its own tile)
     float* tile = reinterpret_cast<float*>(smem);   // [MR][kMmqTilePitch], over the stage buffers
     __syncthreads();
 #pragma unroll
@@ -245,16 +255,61 @@ __global__ void __launch_bounds__(kMmqWarps * 32, 2) q8_mmq_kernel(const MmqArgs
                 (e & 1) ? acc[j][e >> 1].y : acc[j][e >> 1].x;
     namespace cg = cooperative_groups;
     cg::cluster_group cluster = cg::this_cluster();
-    cluster.sync();
+    if (splits > 1) cluster.sync();
+    else __syncthreads();
     const float* peer[kMmqMaxSplits];
 #pragma unroll
     for (int z = 0; z < kMmqMaxSplits; z++)
-        peer[z] = z < splits ? cluster.map_shared_rank(tile, z) : tile;
+        peer[z] = z < splits && splits > 1 ? cluster.map_shared_rank(tile, z) : tile;
+    const int rank = splits > 1 ? (int)cluster.block_rank() : 0;
+    const int nb0 = blockIdx.x * kMmqRows;
+    if (SILU) {
+        // 32-output blocks of the tile (two per activation row: pairs 0-31,
+        // 32-63), whole blocks per CTA; 4 consecutive threads take a block, 8
+        // outputs (16 rows) each, the trip count uniform over the CTA for the
+        // quantizer's shuffles.  Sums in split order, as the plain combine.
+        const int F = a.N / 2, nbf = F / 32;
+        const int nblk = a.M * 2;
+        const int lo = nblk * rank / splits, hi = nblk * (rank + 1) / splits;
+        const int lane = threadIdx.x & 31;
+        for (int base = 4 * lo; base < 4 * hi; base += blockDim.x) {
+            const int u = base + threadIdx.x;
+            const int bk = u >> 2, gq = u & 3;
+            const int m = bk >> 1, hb = bk & 1;
+            const int r0 = 64 * hb + 16 * gq;
+            const bool valid = u < 4 * hi && nb0 + r0 < a.N;
+            float act[8];
+#pragma unroll
+            for (int e = 0; e < 8; e++) {
+                float gs = 0.0f, us = 0.0f;
+                if (valid) {
+                    const int off = m * kMmqTilePitch + r0 + 2 * e;
+                    float pg[kMmqMaxSplits], pu[kMmqMaxSplits];
+#pragma unroll
+                    for (int z = 0; z < kMmqMaxSplits; z++) {
+                        pg[z] = z < splits ? peer[z][off] : 0.0f;
+                        pu[z] = z < splits ? peer[z][off + 1] : 0.0f;
+                    }
+#pragma unroll
+                    for (int z = 0; z < kMmqMaxSplits; z++)
+                        if (z < splits) {
+                            gs = __fadd_rn(gs, pg[z]);
+                            us = __fadd_rn(us, pu[z]);
+                        }
+                }
+                act[e] = __fmul_rn(__fdiv_rn(gs, __fadd_rn(1.0f, expf(-gs))), us);
+            }
+            const int jg = nb0 / 2 + 32 * hb + 8 * gq;   // output index in [0, F)
+            const int b = jg / 32;
+            quant_block_quad(act, lane, valid, a.sq + (int64_t)(valid ? m : 0) * F + (valid ? jg : 0),
+                             a.sdx + (a.sdxt ? (int64_t)b * a.sdxt + m : (int64_t)m * nbf + b));
+        }
+        if (splits > 1) cluster.sync();   // peers' tiles stay alive until every block is read
+        return;
+    }
     // this CTA's slice of the M x 128 outputs, in row-major (m, r) order
     const int total = a.M * kMmqRows;
-    const int rank = (int)cluster.block_rank();
     const int lo = (int)((int64_t)total * rank / splits), hi = (int)((int64_t)total * (rank + 1) / splits);
-    const int nb0 = blockIdx.x * kMmqRows;
     for (int i = lo + threadIdx.x; i < hi; i += blockDim.x) {
         const int m = i / kMmqRows, r = i % kMmqRows;
         const int off = m * kMmqTilePitch + r;

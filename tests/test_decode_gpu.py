@@ -214,10 +214,33 @@ def test_tinyllama_full_workload_runs(cuda):
     d.close()
 
 
+def test_wide_step_fused_silu_is_bit_identical(cuda, monkeypatch):
+    """SiLU*up and its A8 quantization computed in the gate|up product's combine
+    give the same bits as the product into fp32 followed by the SiLU*up kernel:
+    identical logits and tokens over a 32-sequence wide decode, one kernel fewer
+    per layer."""
+    from axion_b200 import ops
+    from axion_b200.decoder import Decoder
+    prompts = np.random.default_rng(21).integers(0, 32000, (32, 5)).astype(np.int32)
+    runs = {}
+    for fused in ("0", "1"):
+        monkeypatch.setenv("AXDEC_SILU_FUSE", fused)   # read when the decoder is created
+        d = Decoder(_tinyllama_cfg(max_batch=32, max_ctx=64))
+        d.init_random(0xA710, std=0.02)
+        toks, lg, _ = d.generate(prompts, 4, logits=True)
+        runs[fused] = (toks, lg, d.step_kernels(32))
+        d.close()
+    assert ops.status() == 0
+    assert np.array_equal(runs["0"][0], runs["1"][0])
+    assert np.array_equal(runs["0"][1], runs["1"][1])
+    assert runs["0"][2] == runs["1"][2] + 22
+
+
 def test_wide_batch_tensor_core_path_matches_single_sequences(cuda):
-    """32 sequences take the wide step (every linear on the tcgen05 product,
-    RoPE/KV and argmax as kernels of their own); each sequence agrees with a
-    single-sequence run of the fused GEMV step (A8 tolerances)."""
+    """32 sequences take the wide step (every linear on the tensor cores, SiLU*up
+    inside the gate|up product, RoPE/KV and argmax as kernels of their own);
+    each sequence agrees with a single-sequence run of the fused GEMV step (A8
+    tolerances)."""
     from axion_b200 import ops
     from axion_b200.decoder import Decoder
     prompts = np.random.default_rng(12).integers(0, 32000, (32, 5)).astype(np.int32)
@@ -227,9 +250,9 @@ def test_wide_batch_tensor_core_path_matches_single_sequences(cuda):
     wide_kernels = d.step_kernels(32)
     d.close()
     assert ops.status() == 0
-    # embed; per layer rmsnorm, qkv, rope/kv, attention, o, rmsnorm, gate|up,
-    # silu, down; final rmsnorm, lm_head, argmax, advance (+ quantization-free products)
-    assert wide_kernels == 1 + 9 * 22 + 4
+    # embed; per layer rmsnorm, qkv, rope/kv, attention, o, rmsnorm, gate|up
+    # (+ SiLU*up -> A8), down; final rmsnorm, lm_head, argmax, advance
+    assert wide_kernels == 1 + 8 * 22 + 4
     # the single-sequence step teacher-forced with the wide run's tokens (a
     # near-tie greedy choice would otherwise fork the continuations)
     d1 = Decoder(_tinyllama_cfg(max_batch=1, max_ctx=64))
