@@ -233,10 +233,74 @@ struct MmqPlan {
     int splits, per;
     int64_t tiles;
 };
+// Clusters of s CTAs of q8_mmq_kernel<MT8> that the device runs at once
+// (cudaOccupancyMaxActiveClusters: clusters are placed whole within a GPC, so
+// this can be below SMs x CTAs per SM / s); 0 when the query fails.  Cached
+// per device.
+template <int MT8>
+int mmq_active_clusters(int dev, int s) {
+    static int cached[kMaxDevices][kMmqMaxSplits + 1] = {};
+    int& v = cached[dev][s];
+    if (v == 0) {
+        int n = 0;
+        if (cudaFuncSetAttribute(q8_mmq_kernel<MT8>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 MmqSmem<MT8>::BYTES) == cudaSuccess) {
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(1, s, 1);
+            cfg.blockDim = dim3(kMmqWarps * 32);
+            cfg.dynamicSmemBytes = MmqSmem<MT8>::BYTES;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = 1;
+            attr[0].val.clusterDim.y = s;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            if (cudaOccupancyMaxActiveClusters(&n, q8_mmq_kernel<MT8>, &cfg) != cudaSuccess) n = 0;
+        }
+        (void)cudaGetLastError();
+        v = n > 0 ? n : -1;
+    }
+    return v > 0 ? v : 0;
+}
+int mmq_active(int dev, int64_t M, int s) {
+    if (M <= 8) return mmq_active_clusters<1>(dev, s);
+    if (M <= 16) return mmq_active_clusters<2>(dev, s);
+    if (M <= 32) return mmq_active_clusters<4>(dev, s);
+    return mmq_active_clusters<8>(dev, s);
+}
+
 MmqPlan mmq_plan(DeviceState* ds, int64_t N, int64_t K, int64_t M) {
     MmqPlan p;
     p.tiles = (N + kMmqRows - 1) / kMmqRows;
     const int nch = (int)((K / 32 + kMmqChunkKb - 1) / kMmqChunkKb);
+    static const bool by_clusters = [] {   // AXQ8_MMQ_PLAN=0: the plain rule below (tuning)
+        const char* e = getenv("AXQ8_MMQ_PLAN");
+        return !(e && atoi(e) == 0);
+    }();
+    const int dev = ds->device >= 0 && ds->device < kMaxDevices ? ds->device : 0;
+    if (by_clusters && mmq_active(dev, M, 1) > 0) {
+        // split count by launch time ~ waves x (chunks per CTA + a fixed two
+        // chunks of start-up and combine), waves counted in clusters that fit
+        const int smax = std::min(kMmqMaxSplits, std::max(1, nch / 2));
+        int64_t best = -1;
+        for (int s = 1; s <= smax; s++) {
+            const int per = (nch + s - 1) / s;
+            const int sp = (nch + per - 1) / per;
+            const int act = mmq_active(dev, M, sp);
+            if (act <= 0) continue;
+            const int64_t waves = (p.tiles + act - 1) / act;
+            const int64_t cost = waves * (per + 2);
+            if (best < 0 || cost < best) {
+                best = cost;
+                p.per = per;
+            }
+        }
+        if (best >= 0) {
+            p.splits = (nch + p.per - 1) / p.per;
+            return p;
+        }
+    }
     const int64_t want = 2 * (int64_t)ds->sm_count;   // two CTAs per SM
     int splits = (int)std::max<int64_t>(1, (want + p.tiles - 1) / p.tiles);
     splits = std::min(splits, std::max(1, nch / 2));   // >= two chunks per split
