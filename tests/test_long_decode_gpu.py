@@ -1,4 +1,4 @@
-"""256 greedy steps against the reference (the north star's decode parity).
+"""256 greedy steps against the reference: logits within 1e-3 and identical tokens.
 
 tests/golden/tinyllama_width_256.npz holds ModelRunner::generate's 256 greedy
 tokens and the per-step logits of the reference (inference/cpp/runtime/
